@@ -1,0 +1,396 @@
+"""Benchmark of the fused attention forward (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c4] [--impl ours|reference]
+
+A step is one forward pass of the workload's attention (every shape of the
+workload, one kernel launch each).  Default workload: the causal
+long-context configuration B=1, H=64, L=16384, D=128, fp16 -- the one the
+metric quotes at 1/2/4/8 GPUs -- with the 64 (batch*head) slices sharded
+contiguously over the ranks (strong scaling: the total work is fixed, each
+rank runs the kernel on its own heads, no collective in the timed region).
+
+Timing: W untimed warm-up steps, then K steps, each bracketed by CUDA events
+on the launching stream; between timed steps a 256 MiB buffer is rewritten to
+flush L2 (outside the events); a barrier and a device synchronise on both
+sides of the timed region; the per-rank total is reduced with MAX.
+
+Reported on the line:
+  value         whole-job TFLOP/s (algorithmic FLOPs of all ranks / max time)
+  e2e           the same metric through the public API ``rocm_attn_op.attn_forward``
+                with pinned HOST inputs: H2D of q/k/v, the forward, D2H of O, all
+                inside the timed region
+  roofline      tensor-bound: TFLOP/s of the kernel launches vs the measured
+                dense bf16 GEMM peak; traffic from the committed ncu summary
+  cpu_baseline  rank 0 at N=1: the reference path (torch SDPA as the
+                reference's _sdpa_fallback runs it) on the host cores, fp32,
+                on a bounded sample of the same workload's heads
+  clocks        nvidia-smi samples taken during the timed region
+``--impl reference`` times that CPU reference path alone on the same
+workload (rank 0; other ranks exit without work).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+if REPO not in sys.path:
+    sys.path.insert(0, REPO)
+
+from rocm_attn_b200.workloads import DTYPES, WORKLOADS, Shape, make_qkv, shard_range  # noqa: E402
+
+METRIC = "attention fwd ms/iter and TFLOPS (% of B200 fp16 TC peak) at 1/2/4/8 GPUs"
+SPEC_DENSE_FP16_TFLOPS = 2250.0
+FALLBACK_PEAK_TFLOPS = 1590.0
+L2_FLUSH_BYTES = 256 << 20
+
+
+def parse_args(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="c4", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--cpu-sample-seconds", type=float, default=12.0)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args(argv)
+
+
+# ---------------------------------------------------------------- helpers
+
+def measured_peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["bf16_tflops"]), float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), "measured"
+    except Exception:
+        return FALLBACK_PEAK_TFLOPS, FALLBACK_PEAK_TFLOPS, "fallback"
+
+
+def profiled_traffic(workload_key: str, rank_heads: int, total_heads: int):
+    """DRAM bytes per launch of the attention kernel, from the committed ncu
+    summary (profiles/attn_fwd_traffic.txt: '<workload> <heads> <bytes>' lines,
+    measured on `heads` slices), scaled to this launch's head count."""
+    p = os.path.join(REPO, "profiles", "attn_fwd_traffic.txt")
+    try:
+        with open(p) as f:
+            for line in f:
+                parts = line.split()
+                if len(parts) == 3 and parts[0] == workload_key:
+                    return float(parts[2]) * rank_heads / float(parts[1])
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.dev = device_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.dev), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.thread.join(timeout=2)
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def local_shapes(workload, world: int, rank: int):
+    """Per-shape (batch*head) range owned by this rank.  Each shape is viewed
+    as [1, B*H, L, D]; the slices of a rank are contiguous."""
+    out = []
+    for s in workload.shapes:
+        r = shard_range(s.bh, world, rank)
+        out.append((s, r))
+    return out
+
+
+def make_local_inputs(workload, shards, seed, device):
+    dtype = DTYPES[workload.dtype]
+    tensors = []
+    for s, r in shards:
+        if len(r) == 0:
+            tensors.append(None)
+            continue
+        g = torch.Generator(device=device)
+        g.manual_seed(seed * 7919 + r.start)
+        shp_q = (1, len(r), s.Lq, s.D)
+        shp_k = (1, len(r), s.Lk, s.D)
+        q = (torch.randn(shp_q, device=device, generator=g) * workload.value_scale).to(dtype)
+        k = (torch.randn(shp_k, device=device, generator=g) * workload.value_scale).to(dtype)
+        v = (torch.randn(shp_k, device=device, generator=g) * workload.value_scale).to(dtype)
+        tensors.append((q, k, v))
+    return tensors
+
+
+# ---------------------------------------------------------------- reference arm
+
+def cpu_reference_sample(workload, seconds: float, seed: int):
+    """Times the reference's CPU path (oracle.reference_sdpa_path, fp32, all
+    host threads) on whole (batch*head) slices of the workload until about
+    `seconds` have elapsed.  Returns (TFLOP/s, cores, sample description)."""
+    import oracle  # CPU reference leg only
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    flops = 0.0
+    t_total = 0.0
+    done = []
+    for s in workload.shapes:
+        per_head = s.flops(workload.causal) / s.bh
+        n = 0
+        for f in range(s.bh):
+            q, k, v = make_qkv(Shape(1, 1, s.Lq, s.Lk, s.D), torch.float32, seed=seed * 131 + f,
+                               value_scale=workload.value_scale)
+            q, k, v = (t.to(DTYPES[workload.dtype]).float() for t in (q, k, v))
+            t0 = time.perf_counter()
+            oracle.reference_sdpa_path(q, k, v, causal=workload.causal)
+            t_total += time.perf_counter() - t0
+            flops += per_head
+            n += 1
+            if t_total >= seconds * (workload.shapes.index(s) + 1) / len(workload.shapes):
+                break
+        done.append(f"{n}/{s.bh} heads of {s.B}x{s.H}x{s.Lq}x{s.Lk}x{s.D}")
+    return flops / t_total / 1e12, cores, "; ".join(done) + f" in {t_total:.1f}s (torch SDPA fp32, CPU)"
+
+
+def run_reference_arm(args, rank, world):
+    w = WORKLOADS[args.workload]
+    if rank != 0:
+        return None
+    per_step = []
+    sample = None
+    cores = os.cpu_count() or 1
+    budget = max(2.0, min(30.0, 120.0 / max(1, args.steps + args.warmup)))
+    for i in range(args.warmup + args.steps):
+        tf, cores, sample = cpu_reference_sample(w, budget, args.seed + i)
+        if i >= args.warmup:
+            per_step.append(tf)
+    value = statistics.median(per_step)
+    ms = w.flops() / (value * 1e12) * 1e3
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "TFLOP/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+        "config": {"workload": w.name, "shapes": [s.__dict__ for s in w.shapes], "causal": w.causal,
+                   "sample": "bounded per step; ms_per_step extrapolated to the whole workload"},
+        "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s", "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    return line
+
+
+# ---------------------------------------------------------------- our arm
+
+def run_ours(args, rank, world, local_rank):
+    import rocm_attn_op  # public API (drop-in name)
+
+    w = WORKLOADS[args.workload]
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream(dev)
+    shards = local_shapes(w, world, rank)
+    inputs = make_local_inputs(w, shards, args.seed, dev)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    dist = torch.distributed if world > 1 else None
+
+    def step():
+        outs = []
+        for t in inputs:
+            if t is not None:
+                outs.append(rocm_attn_op.attn_forward(t[0], t[1], t[2], causal=w.causal))
+        return outs
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize(dev)
+    assert rocm_attn_op.check_status(local_rank) == 0, "kernel watchdog fired during warm-up"
+
+    # ---- timed region (device time, per step events, L2 flushed between steps)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(dev.index) as clk:
+        for i in range(args.steps):
+            flush.fill_(float(i))
+            starts[i].record(stream)
+            step()
+            ends[i].record(stream)
+        torch.cuda.synchronize(dev)
+        if dist:
+            dist.barrier()
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    total_ms = sum(step_ms)
+    t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    max_total_ms = float(t.item())
+    ms_per_step = max_total_ms / args.steps
+    tflops = w.flops() / (ms_per_step * 1e-3) / 1e12
+    assert rocm_attn_op.check_status(local_rank) == 0, "kernel watchdog fired during timing"
+
+    # ---- roofline of the kernel on this rank (one launch per shape per step)
+    local_flops = sum(s.flops(w.causal) * len(r) / s.bh for s, r in shards)
+    local_heads = sum(len(r) for _, r in shards)
+    kernel_tflops = local_flops / (statistics.mean(step_ms) * 1e-3) / 1e12
+    burst, sustained, peak_kind = measured_peaks()
+    traffic = profiled_traffic(args.workload, local_heads, sum(s.bh for s in w.shapes)) if len(w.shapes) == 1 \
+        else None
+    roofline = {"bound": "tensor", "achieved": round(kernel_tflops, 2), "peak": burst, "unit": "TFLOP/s",
+                "frac": round(kernel_tflops / burst, 4), "peak_kind": f"{peak_kind} bf16 dense GEMM (burst)",
+                "frac_of_spec_2250": round(kernel_tflops / SPEC_DENSE_FP16_TFLOPS, 4),
+                "traffic": traffic,
+                "algorithmic_bytes": sum(s.io_bytes() * len(r) / s.bh for s, r in shards)}
+
+    # ---- end to end through the public API with pinned host buffers
+    e2e = None
+    if not args.no_e2e:
+        host_in = []
+        h2d = d2h = 0
+        for t in inputs:
+            if t is None:
+                continue
+            hq, hk, hv = (x.cpu().pin_memory() for x in t)
+            ho = torch.empty(t[0].shape, dtype=t[0].dtype).pin_memory()
+            host_in.append((hq, hk, hv, ho))
+            h2d += sum(x.numel() * x.element_size() for x in (hq, hk, hv))
+            d2h += ho.numel() * ho.element_size()
+        del inputs
+        torch.cuda.empty_cache()
+
+        def e2e_step():
+            for hq, hk, hv, ho in host_in:
+                q = hq.to(dev, non_blocking=True)
+                k = hk.to(dev, non_blocking=True)
+                v = hv.to(dev, non_blocking=True)
+                o = rocm_attn_op.attn_forward(q, k, v, causal=w.causal)
+                ho.copy_(o, non_blocking=True)
+
+        e2e_step()
+        torch.cuda.synchronize(dev)
+        n_e2e = max(3, min(args.steps, 10))
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        ev0.record(stream)
+        for _ in range(n_e2e):
+            e2e_step()
+        ev1.record(stream)
+        torch.cuda.synchronize(dev)
+        e_ms = torch.tensor([ev0.elapsed_time(ev1) / n_e2e], dtype=torch.float64, device=dev)
+        if dist:
+            dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
+        e2e = {"value": round(w.flops() / (float(e_ms.item()) * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
+               "ms_per_step": round(float(e_ms.item()), 3), "h2d_bytes_per_step": int(h2d),
+               "d2h_bytes_per_step": int(d2h), "steps": n_e2e}
+
+    clocks = clk.summary()
+    line = {
+        "metric": METRIC, "value": round(tflops, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": w.dtype, "data": "synthetic",
+        "config": {"workload": w.name, "shapes": [s.__dict__ for s in w.shapes], "causal": w.causal,
+                   "sharding": "contiguous (batch*head) slices per rank, no collective in the timed region",
+                   "l2": "256 MiB buffer rewritten between timed steps (outside the events)",
+                   "frac_of_spec_dense_fp16": round(tflops / world / SPEC_DENSE_FP16_TFLOPS, 4)},
+        "e2e": e2e,
+        "gpu_launches": args.steps * sum(1 for _, r in shards if len(r) > 0),
+        "roofline": roofline,
+        "clocks": clocks,
+    }
+    return line
+
+
+def main(argv=None):
+    args = parse_args(argv)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE={world}; using WORLD_SIZE", file=sys.stderr)
+    dist = None
+    if world > 1 and args.impl == "ours":
+        import datetime
+        torch.cuda.set_device(local_rank)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                             device_id=torch.device("cuda", local_rank))
+        dist = torch.distributed
+    try:
+        if args.impl == "reference":
+            line = run_reference_arm(args, rank, world)
+        else:
+            line = run_ours(args, rank, world, local_rank)
+            if rank == 0 and world == 1 and not args.no_cpu_baseline:
+                tf, cores, sample = cpu_reference_sample(WORKLOADS[args.workload], args.cpu_sample_seconds,
+                                                         args.seed)
+                line["cpu_baseline"] = {"value": round(tf, 4), "unit": "TFLOP/s", "cores": cores, "kind": "port",
+                                        "sample": sample}
+        if rank == 0 and line is not None:
+            print(json.dumps(line), flush=True)
+    finally:
+        if dist is not None:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,87 @@
+/*
+ * C-ABI launch interface of the sm_100a attention-forward library
+ * (librocm_attn.so).  Plain pointers and sizes only; no framework types.
+ *
+ * Replaces the reference's `launch_attn_forward` declared at
+ * src/attn_kernel.h:18-20 of JoursBleu/rocm_attn (enum AttnDType at
+ * src/attn_kernel.h:12-16), whose definitions live at
+ * src/attn_kernel_torch.cu:625-689 and src/attn_kernel.hip.cpp:304-367.
+ *
+ * Differences from the reference signature, all deliberate:
+ *   - returns an int status (the reference returns void and checks nothing);
+ *   - takes an explicit softmax scale (the reference hard-wires rsqrt(D),
+ *     src/attn_kernel_torch.cu:111); a value <= 0 or non-finite selects the
+ *     reference default 1/sqrt(D);
+ *   - the stream is a cudaStream_t (the reference takes a hipStream_t).
+ * The argument order otherwise matches the reference.
+ */
+#ifndef ROCM_ATTN_B200_ATTN_KERNEL_H_
+#define ROCM_ATTN_B200_ATTN_KERNEL_H_
+
+#include <cuda_runtime.h>
+#include <stdbool.h>
+
+#if defined(__GNUC__)
+#define ATTN_API __attribute__((visibility("default")))
+#else
+#define ATTN_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Element type of q/k/v/out.  Values match the reference enum
+ * (src/attn_kernel.h:12-16) so the ABI stays compatible. */
+typedef enum AttnDType {
+  ATTN_F16 = 0,
+  ATTN_BF16 = 1,
+  ATTN_F32 = 2,
+} AttnDType;
+
+/* Status codes returned by the entry points below. */
+enum AttnStatus {
+  ATTN_OK = 0,
+  ATTN_ERR_INVALID_ARGUMENT = 1, /* null pointer, negative size, overflow   */
+  ATTN_ERR_UNSUPPORTED = 2,      /* dtype / head_dim not built              */
+  ATTN_ERR_MISALIGNED = 3,       /* pointer not 16-byte aligned             */
+  ATTN_ERR_TENSOR_MAP = 4,       /* TMA descriptor could not be encoded     */
+  ATTN_ERR_LAUNCH = 5,           /* CUDA runtime error at launch            */
+  ATTN_ERR_DEVICE = 6,           /* current device is not an sm_100 GPU     */
+  ATTN_ERR_WATCHDOG = 7          /* a kernel wait timed out (see below)     */
+};
+
+/*
+ * Scaled dot-product attention forward, O = softmax(scale * Q K^T [+ mask]) V.
+ *   q   [B, H, Sq,  D]  contiguous, row-major
+ *   k,v [B, H, Skv, D]  contiguous, row-major
+ *   out [B, H, Sq,  D]  contiguous, row-major, fully overwritten
+ * causal: key j is masked for query i when j > i (top-left aligned, the
+ * reference's rule at src/attn_kernel_torch.cu:54,238,263).  Skv == 0 gives
+ * an all-zero output, like the reference's empty-denominator rule
+ * (src/attn_kernel_torch.cu:335-336).
+ * Supported: dtype ATTN_F16 / ATTN_BF16, D in {64, 128}; all pointers 16-byte
+ * aligned.  Asynchronous on `stream`; allocates nothing; re-entrant.
+ * Returns ATTN_OK or an AttnStatus code; on error nothing was launched.
+ */
+ATTN_API int launch_attn_forward(const void* q, const void* k, const void* v, void* out, int B, int H, int Sq, int Skv,
+                        int D, bool causal, float softmax_scale, AttnDType dtype, cudaStream_t stream);
+
+/*
+ * Reads and clears the device status word of the current device, after
+ * synchronising `stream`.  *status receives ATTN_OK, or ATTN_WATCHDOG when a
+ * kernel launched earlier gave up on a wait (its output is then invalid).
+ * No counterpart in the reference, whose launcher has no error reporting.
+ * Returns ATTN_OK, or ATTN_ERR_LAUNCH if the synchronisation itself failed.
+ */
+ATTN_API int attn_get_status(cudaStream_t stream, int* status);
+
+/* Library version, major * 10000 + minor * 100 + patch.  No reference
+ * counterpart; lets a binding check which build it loaded. */
+ATTN_API int attn_library_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ROCM_ATTN_B200_ATTN_KERNEL_H_ */

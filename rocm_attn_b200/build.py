@@ -1,0 +1,128 @@
+"""In-tree build of the native parts.
+
+* ``librocm_attn.so``  -- the sm_100a kernels and the C-ABI launcher
+  (``csrc/attn_kernel.cu``), compiled by nvcc for ``sm_100a`` only, with the
+  CUDA runtime linked statically so the library loads without torch.
+* ``rocm_attn_ext*.so`` -- the PyTorch binding (``csrc/attn_torch.cpp``),
+  linked against ``librocm_attn.so`` through an ``$ORIGIN`` rpath.
+
+Both land next to this file so they travel with the source tree.  Run as
+``python rocm_attn_b200/build.py`` (or through ``__graft_entry__.build()``).
+"""
+from __future__ import annotations
+
+import os
+import shutil
+import subprocess
+import sys
+import sysconfig
+
+PKG_DIR = os.path.dirname(os.path.abspath(__file__))
+REPO_DIR = os.path.dirname(PKG_DIR)
+CSRC = os.path.join(PKG_DIR, "csrc")
+INCLUDE = os.path.join(REPO_DIR, "include")
+KERNEL_LIB = os.path.join(PKG_DIR, "librocm_attn.so")
+
+NVCC_FLAGS = [
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "-O3", "-std=c++17", "-lineinfo",
+    "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
+    "-cudart", "static",
+]
+
+
+def _nvcc() -> str:
+    for cand in (os.environ.get("NVCC"), shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
+        if cand and os.path.exists(cand):
+            return cand
+    raise RuntimeError("nvcc not found; the sm_100a kernels need the CUDA toolkit to build")
+
+
+def _newer(target: str, sources: list[str]) -> bool:
+    if not os.path.exists(target):
+        return True
+    t = os.path.getmtime(target)
+    return any(os.path.getmtime(s) > t for s in sources)
+
+
+def _kernel_sources() -> list[str]:
+    return [os.path.join(CSRC, f) for f in sorted(os.listdir(CSRC))
+            if f.endswith((".cu", ".cuh", ".h"))] + [os.path.join(INCLUDE, "attn_kernel.h")]
+
+
+def build_kernel_lib(force: bool = False, verbose: bool = False) -> str:
+    """Compile csrc/attn_kernel.cu into librocm_attn.so (sm_100a)."""
+    if not force and not _newer(KERNEL_LIB, _kernel_sources()):
+        return KERNEL_LIB
+    cmd = [_nvcc(), *NVCC_FLAGS, "-I", INCLUDE, "-shared",
+           os.path.join(CSRC, "attn_kernel.cu"), "-o", KERNEL_LIB + ".tmp"]
+    if verbose:
+        cmd.insert(1, "-Xptxas=-v")
+    subprocess.run(cmd, check=True)
+    os.replace(KERNEL_LIB + ".tmp", KERNEL_LIB)
+    return KERNEL_LIB
+
+
+def ext_path() -> str | None:
+    suffix = sysconfig.get_config_var("EXT_SUFFIX") or ".so"
+    p = os.path.join(PKG_DIR, "rocm_attn_ext" + suffix)
+    return p if os.path.exists(p) else None
+
+
+def build_torch_ext(force: bool = False) -> str:
+    """Build the PyTorch binding in place (rocm_attn_b200/rocm_attn_ext*.so)."""
+    src = os.path.join(CSRC, "attn_torch.cpp")
+    existing = ext_path()
+    if not force and existing and not _newer(existing, [src, KERNEL_LIB, os.path.join(INCLUDE, "attn_kernel.h")]):
+        return existing
+    from setuptools import setup
+    from torch.utils.cpp_extension import BuildExtension, CUDAExtension
+
+    build_temp = os.path.join(PKG_DIR, "_build")
+    ext = CUDAExtension(
+        name="rocm_attn_b200.rocm_attn_ext",
+        sources=[os.path.relpath(src, REPO_DIR)],
+        include_dirs=[INCLUDE],
+        library_dirs=[PKG_DIR],
+        libraries=["rocm_attn"],
+        extra_compile_args={"cxx": ["-O3"]},
+        extra_link_args=["-Wl,-rpath,$ORIGIN"],
+    )
+    # Link against the system libstdc++ the rest of the process (torch) uses.
+    # A toolchain wrapper that resolves -lstdc++ to a partial static copy puts
+    # a second set of iostream/locale internals into the module, and the first
+    # `ostream << int` on an error path then crashes in a mismatched facet.
+    env_save = {k: os.environ.get(k) for k in ("CXX", "CC")}
+    for var, exe in (("CXX", "/usr/bin/g++"), ("CC", "/usr/bin/gcc")):
+        if os.path.exists(exe):
+            os.environ[var] = exe
+    cwd = os.getcwd()
+    os.chdir(REPO_DIR)
+    try:
+        setup(
+            name="rocm_attn_b200_ext",
+            ext_modules=[ext],
+            cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
+            script_args=["-q", "build_ext", "--inplace", "--build-temp", build_temp],
+        )
+    finally:
+        os.chdir(cwd)
+        for k, v in env_save.items():
+            if v is None:
+                os.environ.pop(k, None)
+            else:
+                os.environ[k] = v
+    p = ext_path()
+    if p is None:
+        raise RuntimeError("PyTorch extension build produced no module")
+    return p
+
+
+def build_all(force: bool = False, verbose: bool = False) -> None:
+    build_kernel_lib(force=force, verbose=verbose)
+    build_torch_ext(force=force)
+
+
+if __name__ == "__main__":
+    build_all(force="--force" in sys.argv, verbose="-v" in sys.argv)
+    print("built", KERNEL_LIB, ext_path())

@@ -1,0 +1,58 @@
+"""Host-side logic: workload definitions, FLOP accounting, seeding, sharding."""
+import pytest
+import torch
+
+from rocm_attn_b200.workloads import WORKLOADS, Shape, make_qkv, parse_shapes, shard_range, slice_seed
+from rocm_attn_b200.sharding import local_view
+
+
+def test_config_flops():
+    # 4*B*H*Lq*Lk*D non-causal; causal counts exactly the unmasked pairs
+    assert WORKLOADS["c1"].flops() == pytest.approx(68.72e9, rel=1e-3)
+    assert WORKLOADS["c2"].flops() == pytest.approx(4 * 32 * 128 * 2048 * 2049 / 2)
+    assert WORKLOADS["c3"].flops() == pytest.approx(34.36e9, rel=1e-3)
+    assert WORKLOADS["c4"].flops() == pytest.approx(4 * 64 * 128 * 16384 * 16385 / 2)
+    assert WORKLOADS["c5"].flops() == pytest.approx(1380.3e9, rel=1e-3)
+
+
+def test_causal_pairs_cross_shapes():
+    assert Shape(1, 1, 4, 6, 8).unmasked_pairs(True) == 1 + 2 + 3 + 4
+    assert Shape(1, 1, 6, 4, 8).unmasked_pairs(True) == 1 + 2 + 3 + 4 + 4 + 4
+
+
+def test_parse_shapes_reference_syntax():
+    # benchmark/bench_attention.py:25-44 syntax, e.g. the preset file entries
+    s = parse_shapes("2560,8,16,64;16,5,2560,93,64")
+    assert s == [Shape(2560, 8, 16, 16, 64), Shape(16, 5, 2560, 93, 64)]
+    with pytest.raises(ValueError):
+        parse_shapes("1,2,3")
+    with pytest.raises(ValueError):
+        parse_shapes(" ; ")
+
+
+@pytest.mark.parametrize("n,world", [(64, 1), (64, 8), (32, 3), (5, 8), (1, 2)])
+def test_shard_range_partitions(n, world):
+    parts = [shard_range(n, world, r) for r in range(world)]
+    flat = [i for p in parts for i in p]
+    assert flat == list(range(n))
+    sizes = [len(p) for p in parts]
+    assert max(sizes) - min(sizes) <= 1
+
+
+def test_slice_seeds_distinct_and_inputs_deterministic():
+    seeds = {slice_seed(0, t, b, h) for t in "qkv" for b in range(4) for h in range(16)}
+    assert len(seeds) == 3 * 4 * 16
+    s = Shape(2, 3, 10, 12, 64)
+    a = make_qkv(s, torch.float16, seed=1)
+    b = make_qkv(s, torch.float16, seed=1)
+    assert all(torch.equal(x, y) for x, y in zip(a, b))
+    # a rank can regenerate its own heads without the rest
+    part = make_qkv(s, torch.float16, seed=1, bh_range=range(2, 5))
+    for full, p in zip(a, part):
+        assert torch.equal(full.reshape(1, 6, *full.shape[2:])[:, 2:5], p)
+
+
+def test_local_view_is_a_view():
+    t = torch.arange(2 * 3 * 4 * 8, dtype=torch.float32).view(2, 3, 4, 8)
+    v = local_view(t, 4, 1)
+    assert v.shape == (1, 2, 4, 8) and v.data_ptr() == t[0, 1].data_ptr()
