@@ -34,7 +34,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -45,7 +44,8 @@ REPO = os.path.dirname(os.path.abspath(__file__))
 if REPO not in sys.path:
     sys.path.insert(0, REPO)
 
-from rocm_attn_b200.workloads import DTYPES, WORKLOADS, Shape, make_qkv, shard_range  # noqa: E402
+from rocm_attn_b200.workloads import (DTYPES, WORKLOADS, Shape, Workload, make_qkv, parse_shapes,  # noqa: E402
+                                      shard_range)
 
 METRIC = "attention fwd ms/iter and TFLOPS (% of B200 fp16 TC peak) at 1/2/4/8 GPUs"
 SPEC_DENSE_FP16_TFLOPS = 2250.0
@@ -58,7 +58,12 @@ def parse_args(argv=None):
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", default="c4", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="c4", choices=sorted(WORKLOADS) + ["custom"])
+    ap.add_argument("--shapes", default=None,
+                    help="custom workload: 'B,H,Lq,D' or 'B,H,Lq,Lk,D' entries separated by ';' "
+                         "(the reference benchmark's --shapes syntax); implies --workload custom")
+    ap.add_argument("--causal", action="store_true", help="custom workload: causal masking")
+    ap.add_argument("--dtype", default="fp16", choices=["fp16", "bf16"], help="custom workload dtype")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--cpu-sample-seconds", type=float, default=12.0)
@@ -96,59 +101,62 @@ def profiled_traffic(workload_key: str, rank_heads: int, total_heads: int):
 
 
 class ClockSampler:
-    """nvidia-smi sampling of SM clocks and throttle reasons while running."""
+    """Samples SM clock, max clock and clock-event (throttle) reasons of one
+    GPU every few milliseconds through NVML while the timed region runs."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown"}
 
-    def __init__(self, device_index: int):
+    def __init__(self, device_index: int, period_s: float = 0.002):
         self.dev = device_index
-        self.proc = None
-        self.lines = []
+        self.period = period_s
+        self.samples = []
+        self._stop = threading.Event()
+        self.max_mhz = None
+        self.error = None
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.dev), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
-            self.thread.start()
-        except OSError:
-            self.proc = None
+            import pynvml
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(self.dev)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM))
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        except Exception as e:  # NVML missing: report no samples rather than fail the bench
+            self._nvml = None
+            self.error = repr(e)
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+    def _run(self):
+        nv = self._nvml
+        while not self._stop.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
+                reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                self.samples.append((float(sm), int(reasons)))
+            except Exception as e:
+                self.error = repr(e)
+                return
+            time.sleep(self.period)
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
+        self._stop.set()
+        if self._nvml is not None:
+            self._thread.join(timeout=2)
             try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-            self.thread.join(timeout=2)
+                self._nvml.nvmlShutdown()
+            except Exception:
+                pass
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            f = [x.strip() for x in ln.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        reasons = sorted({name for _, r in self.samples for bit, name in self.REASONS.items() if r & bit})
+        out = {"sm_mhz": statistics.median([c for c, _ in self.samples]) if self.samples else None,
+               "sm_max_mhz": self.max_mhz, "reasons": reasons, "samples": len(self.samples), "source": "nvml"}
+        if self.error and not self.samples:
+            out["error"] = self.error
+        return out
 
 
 def local_shapes(workload, world: int, rank: int):
@@ -363,6 +371,12 @@ def run_ours(args, rank, world, local_rank):
 
 def main(argv=None):
     args = parse_args(argv)
+    if args.shapes:
+        WORKLOADS["custom"] = Workload("custom-" + args.shapes.replace(";", "_") + ("-causal" if args.causal else "")
+                                       + "-" + args.dtype, tuple(parse_shapes(args.shapes)), args.dtype, args.causal)
+        args.workload = "custom"
+    elif args.workload == "custom":
+        raise SystemExit("--workload custom needs --shapes")
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
