@@ -39,6 +39,25 @@ namespace ra {
 // Sticky per-device status word written by the kernel's watchdog.
 __device__ int g_attn_status = 0;
 
+// Optional device-side timeline of one CTA (build with -DRA_TRACE): lane 0 of
+// each role writes %clock64 at fixed points of every key block into
+// g_attn_trace, read back with attn_trace_read().  Compiled out by default.
+#ifdef RA_TRACE
+constexpr int kTraceSlots = 8192;
+__device__ unsigned long long g_attn_trace[kTraceSlots];
+__device__ int g_attn_trace_cta = 0;
+#define RA_MARK(idx)                                                                      \
+  do {                                                                                    \
+    if ((threadIdx.x & 31) == 0 && static_cast<int>(blockIdx.x) == g_attn_trace_cta &&    \
+        (idx) < kTraceSlots)                                                              \
+      g_attn_trace[(idx)] = clock64();                                                    \
+  } while (0)
+#else
+#define RA_MARK(idx) \
+  do {               \
+  } while (0)
+#endif
+
 enum : int { kWatchQ = 0x10, kWatchK = 0x20, kWatchV = 0x30, kWatchS = 0x40, kWatchP = 0x50, kWatchO = 0x60,
              kWatchDrain = 0x70 };
 
@@ -47,27 +66,43 @@ struct AttnParams {
   int Lk;           // key rows per (batch, head)
   int BH;           // batch * heads
   int num_qblocks;  // ceil(Lq / 256)
+  int head_group;   // causal: heads per scheduling group (their K/V fit in L2)
   float scale_log2; // softmax scale * log2(e)
 };
 
+// Compile-time shape of the pipeline for head dimension kD.
 template <int kD>
 struct Cfg {
-  static constexpr int kBM = 128;                       // rows per Q tile
+  static constexpr int kBM = 128;                       // rows per Q tile (2 tiles per CTA)
   static constexpr int kBN = 128;                       // keys per block
   static constexpr int kStagesK = kD == 128 ? 2 : 3;    // K ring depth
   static constexpr int kStagesV = kD == 128 ? 2 : 3;    // V ring depth
   static constexpr uint32_t kTileBytes = 128u * kD * 2; // one 128 x D tile
+  static constexpr uint32_t kBlockBytes = 128u * 128;   // one 64-column block of a tile
   static constexpr uint32_t kSmemBytes = 1024 + 2 * kTileBytes + (kStagesK + kStagesV) * kTileBytes;
   static constexpr uint32_t kTmemCols = 512;
   static constexpr uint32_t kColO = 256;
   static constexpr int kThreads = 320;
 };
 
+// Fraction of the softmax exponentials evaluated by the FMA-pipe polynomial
+// (exp2_poly2) instead of the MUFU: pairs i with (i % kPolyDen) < kPolyNum.
+#ifndef RA_POLY_NUM
+#define RA_POLY_NUM 1
+#endif
+#ifndef RA_POLY_DEN
+#define RA_POLY_DEN 4
+#endif
+constexpr int kPolyNum = RA_POLY_NUM;
+constexpr int kPolyDen = RA_POLY_DEN;
+
 struct __align__(8) SharedCtl {
   uint64_t q_full;
   uint64_t k_full[3], k_empty[3];
   uint64_t v_full[3], v_empty[3];
-  uint64_t s_full[2], p_full[2], o_full[2];
+  uint64_t s_full[2];     // [tile]: S(j) computed
+  uint64_t p_full[2][2];  // [tile][64-key half]: P(j) half stored (128 arrivals)
+  uint64_t o_full[2];     // [tile]: the last P*V product retired
   uint64_t mma_done;
   uint32_t tmem_base;
   int abort_flag;
@@ -81,6 +116,27 @@ __device__ __forceinline__ int tile_key_blocks(int q0, int t, int Lq, int Lk, bo
   if (!causal) return all;
   const int last = min(first + 127, Lq - 1);
   return min(all, last / 128 + 1);
+}
+
+// exp2 of 32 consecutive scores (relative to the reference point -nmc2/c2),
+// packed to 16-bit pairs; returns the fp32 sum of the exponentials in `sum2`.
+template <bool kBf16, int kSrc, int kDst>
+__device__ __forceinline__ void exp_pack32(const float (&s)[128], uint64_t c2, uint64_t nmc2, uint32_t (&pk)[32],
+                                           uint64_t& sum2) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const uint64_t x = f2_fma(f2(s[kSrc + 2 * i], s[kSrc + 2 * i + 1]), c2, nmc2);
+    float x0, x1, a, b;
+    f2_split(x, x0, x1);
+    if ((i % kPolyDen) < kPolyNum) {
+      exp2_poly2(x0, x1, a, b);  // FMA pipe
+    } else {
+      a = ex2_approx(x0);        // MUFU
+      b = ex2_approx(x1);
+    }
+    sum2 = f2_add(sum2, f2(a, b));
+    pk[kDst + i] = pack2<kBf16>(a, b);
+  }
 }
 
 template <bool kBf16, int kD, bool kCausal>
@@ -101,9 +157,24 @@ __global__ void __launch_bounds__(320, 1)
   const int warp = __shfl_sync(0xffffffffu, static_cast<int>(threadIdx.x) / 32, 0);
   const int lane = threadIdx.x & 31;
 
-  // Work unit: heads in order, the longest (last) query blocks of a head first.
-  const int bh = blockIdx.x / p.num_qblocks;
-  const int qb = p.num_qblocks - 1 - static_cast<int>(blockIdx.x % p.num_qblocks);
+  // Work unit (bh, qb).  Non-causal: every unit costs the same; the query
+  // blocks of a head are adjacent so its K/V stay hot in L2.  Causal: unit
+  // cost grows with qb, so all heads' longest query blocks go first (longest
+  // processing time first keeps the last wave short).
+  int bh, qb;
+  if (kCausal) {
+    // Groups of head_group heads in sequence; inside a group, all query
+    // blocks of its heads in longest-first order.
+    const int per_group = p.head_group * p.num_qblocks;
+    const int g = static_cast<int>(blockIdx.x) / per_group;
+    const int r = static_cast<int>(blockIdx.x) - g * per_group;
+    const int heads = min(p.head_group, p.BH - g * p.head_group);
+    qb = p.num_qblocks - 1 - r / heads;
+    bh = g * p.head_group + r % heads;
+  } else {
+    bh = blockIdx.x / p.num_qblocks;
+    qb = p.num_qblocks - 1 - static_cast<int>(blockIdx.x % p.num_qblocks);
+  }
   const int q0 = qb * 256;
   const int n0 = tile_key_blocks(q0, 0, p.Lq, p.Lk, kCausal);
   const int n1 = tile_key_blocks(q0, 1, p.Lq, p.Lk, kCausal);
@@ -120,7 +191,8 @@ __global__ void __launch_bounds__(320, 1)
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&ctl.s_full[t], 1);
-      mbar_init(&ctl.p_full[t], 128);
+      mbar_init(&ctl.p_full[t][0], 128);
+      mbar_init(&ctl.p_full[t][1], 128);
       mbar_init(&ctl.o_full[t], 1);
     }
     mbar_init(&ctl.mma_done, 1);
@@ -141,6 +213,7 @@ __global__ void __launch_bounds__(320, 1)
   tc_fence_after();
   const uint32_t tmem = ctl.tmem_base;
 
+  RA_MARK(8190 - warp);
   if (warp == 9) {
     // ------------------------------------------------------------------ TMA
     const uint64_t pol_stream = l2_policy_evict_first();
@@ -151,33 +224,36 @@ __global__ void __launch_bounds__(320, 1)
       mbar_arrive_expect_tx(&ctl.q_full, (n1 > 0 ? 2u : 1u) * C::kTileBytes);
       for (int t = 0; t < (n1 > 0 ? 2 : 1); ++t)
         for (int cb = 0; cb < kD / 64; ++cb)
-          tma_load_3d(smem_addr(sQ + t * C::kTileBytes + cb * 16384), &map_q, &ctl.q_full, cb * 64,
+          tma_load_3d(smem_addr(sQ + t * C::kTileBytes + cb * C::kBlockBytes), &map_q, &ctl.q_full, cb * 64,
                       q0 + t * 128, bh, pol_stream);
     }
     bool ok = true;
     for (int j = 0; j < nkb && ok; ++j) {
       const int sk = j % C::kStagesK;
-      ok = mbar_wait(&ctl.k_empty[sk], ((j / C::kStagesK) & 1) ^ 1, abort_flag, status, kWatchK + 1);
-      ok = __all_sync(0xffffffffu, ok);
+      RA_MARK(6144 + j * 4 + 0);
+      ok = __all_sync(0xffffffffu,
+                      mbar_wait(&ctl.k_empty[sk], ((j / C::kStagesK) & 1) ^ 1, abort_flag, status, kWatchK + 1));
       if (!ok) break;
       if (leader) {
         mbar_arrive_expect_tx(&ctl.k_full[sk], C::kTileBytes);
         for (int cb = 0; cb < kD / 64; ++cb)
-          tma_load_3d(smem_addr(sK + sk * C::kTileBytes + cb * 16384), &map_k, &ctl.k_full[sk], cb * 64,
+          tma_load_3d(smem_addr(sK + sk * C::kTileBytes + cb * C::kBlockBytes), &map_k, &ctl.k_full[sk], cb * 64,
                       j * 128, bh, pol_keep);
       }
       last_k[sk] = j;
+      RA_MARK(6144 + j * 4 + 1);
       const int sv = j % C::kStagesV;
-      ok = mbar_wait(&ctl.v_empty[sv], ((j / C::kStagesV) & 1) ^ 1, abort_flag, status, kWatchV + 1);
-      ok = __all_sync(0xffffffffu, ok);
+      ok = __all_sync(0xffffffffu,
+                      mbar_wait(&ctl.v_empty[sv], ((j / C::kStagesV) & 1) ^ 1, abort_flag, status, kWatchV + 1));
       if (!ok) break;
       if (leader) {
         mbar_arrive_expect_tx(&ctl.v_full[sv], C::kTileBytes);
         for (int cb = 0; cb < kD / 64; ++cb)
-          tma_load_3d(smem_addr(sV + sv * C::kTileBytes + cb * 16384), &map_v, &ctl.v_full[sv], cb * 64,
+          tma_load_3d(smem_addr(sV + sv * C::kTileBytes + cb * C::kBlockBytes), &map_v, &ctl.v_full[sv], cb * 64,
                       j * 128, bh, pol_keep);
       }
       last_v[sv] = j;
+      RA_MARK(6144 + j * 4 + 2);
     }
     if (!ok) {
       // Aborted: let every copy already issued land before the CTA exits.
@@ -201,25 +277,41 @@ __global__ void __launch_bounds__(320, 1)
     auto issue_s = [&](uint32_t d_tmem, uint32_t q_addr, uint32_t k_addr) {
 #pragma unroll
       for (int k = 0; k < kD / 16; ++k) {
-        const uint32_t off = (k / 4) * 16384 + (k % 4) * 32;
+        const uint32_t off = (k / 4) * C::kBlockBytes + (k % 4) * 32;
         umma_ss(d_tmem, sw128_desc(q_addr + off, 16, 1024), sw128_desc(k_addr + off, 16, 1024), idesc_s,
                 k > 0 ? 1u : 0u);
       }
     };
-    // O (+)= P V over 128 keys in steps of 16 (P from TMEM, V MN-major).
-    auto issue_o = [&](uint32_t d_tmem, uint32_t p_tmem, uint32_t v_addr, bool acc) {
+    // O (+)= P V over 128 keys in steps of 16 (P from TMEM, V MN-major).  The
+    // two 64-key halves wait for their own half of P, so the first half of
+    // the product overlaps the softmax of the second half.
+    auto issue_pv = [&](int t, uint32_t v_addr, bool acc, uint32_t parity, int code) -> bool {
+      const uint32_t d_tmem = t == 0 ? tO0 : tO1;
+      const uint32_t p_tmem = t == 0 ? tS0 : tS1;
 #pragma unroll
-      for (int k = 0; k < 8; ++k)
-        umma_ts(d_tmem, p_tmem + k * 8, sw128_desc(v_addr + k * 2048, 16384, 1024), idesc_o,
-                (acc || k > 0) ? 1u : 0u);
+      for (int h = 0; h < 2; ++h) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&ctl.p_full[t][h], parity, abort_flag, status, code + h)))
+          return false;
+        tc_fence_after();
+        if (leader) {
+#pragma unroll
+          for (int k = 4 * h; k < 4 * h + 4; ++k)
+            umma_ts(d_tmem, p_tmem + k * 8, sw128_desc(v_addr + k * 2048, C::kBlockBytes, 1024), idesc_o,
+                    (acc || k > 0) ? 1u : 0u);
+        }
+        __syncwarp();
+      }
+      return true;
     };
 
-    bool ok = mbar_wait(&ctl.q_full, 0, abort_flag, status, kWatchQ + 2);
-    ok = __all_sync(0xffffffffu, ok);
+    bool ok = __all_sync(0xffffffffu, mbar_wait(&ctl.q_full, 0, abort_flag, status, kWatchQ + 2));
+    // Issue order per key block j: S0(j), O1 += P1(j-1) V(j-1), S1(j), O0 += P0(j) V(j).
     for (int j = 0; j < nkb && ok; ++j) {
       const int sk = j % C::kStagesK, sv = j % C::kStagesV;
       const uint32_t k_addr = smem_addr(sK + sk * C::kTileBytes);
-      ok = __all_sync(0xffffffffu, mbar_wait(&ctl.k_full[sk], (j / C::kStagesK) & 1, abort_flag, status, kWatchK + 2));
+      RA_MARK(4096 + j * 8 + 0);
+      ok = __all_sync(0xffffffffu,
+                      mbar_wait(&ctl.k_full[sk], (j / C::kStagesK) & 1, abort_flag, status, kWatchK + 2));
       if (!ok) break;
       tc_fence_after();
       if (leader && j < n0) {
@@ -227,17 +319,15 @@ __global__ void __launch_bounds__(320, 1)
         umma_commit(&ctl.s_full[0]);
       }
       __syncwarp();
+      RA_MARK(4096 + j * 8 + 1);
       if (j >= 1 && j - 1 < n1) {
-        ok = __all_sync(0xffffffffu, mbar_wait(&ctl.p_full[1], (j - 1) & 1, abort_flag, status, kWatchP + 2));
-        if (!ok) break;
-        tc_fence_after();
         const int pv = (j - 1) % C::kStagesV;
-        if (leader) {
-          issue_o(tO1, tS1, smem_addr(sV + pv * C::kTileBytes), j - 1 > 0);
-          umma_commit(&ctl.v_empty[pv]);
-        }
+        ok = issue_pv(1, smem_addr(sV + pv * C::kTileBytes), j - 1 > 0, (j - 1) & 1, kWatchP + 2);
+        if (!ok) break;
+        if (leader) umma_commit(&ctl.v_empty[pv]);
         __syncwarp();
       }
+      RA_MARK(4096 + j * 8 + 2);
       if (leader) {
         if (j < n1) {
           issue_s(tS1, q_addr1, k_addr);
@@ -246,33 +336,28 @@ __global__ void __launch_bounds__(320, 1)
         umma_commit(&ctl.k_empty[sk]);
       }
       __syncwarp();
-      ok = __all_sync(0xffffffffu, mbar_wait(&ctl.v_full[sv], (j / C::kStagesV) & 1, abort_flag, status, kWatchV + 2));
+      RA_MARK(4096 + j * 8 + 3);
+      ok = __all_sync(0xffffffffu,
+                      mbar_wait(&ctl.v_full[sv], (j / C::kStagesV) & 1, abort_flag, status, kWatchV + 2));
       if (!ok) break;
       if (j < n0) {
-        ok = __all_sync(0xffffffffu, mbar_wait(&ctl.p_full[0], j & 1, abort_flag, status, kWatchP + 1));
+        ok = issue_pv(0, smem_addr(sV + sv * C::kTileBytes), j > 0, j & 1, kWatchP + 0);
         if (!ok) break;
-        tc_fence_after();
-        if (leader) {
-          issue_o(tO0, tS0, smem_addr(sV + sv * C::kTileBytes), j > 0);
-          if (j == n0 - 1) umma_commit(&ctl.o_full[0]);
-        }
+        if (leader && j == n0 - 1) umma_commit(&ctl.o_full[0]);
         __syncwarp();
       }
+      RA_MARK(4096 + j * 8 + 4);
       if (leader && j >= n1) umma_commit(&ctl.v_empty[sv]);
       __syncwarp();
     }
     if (ok && n1 > 0 && n1 == nkb) {
-      ok = __all_sync(0xffffffffu, mbar_wait(&ctl.p_full[1], (nkb - 1) & 1, abort_flag, status, kWatchP + 3));
-      if (ok) {
-        tc_fence_after();
-        const int pv = (nkb - 1) % C::kStagesV;
-        if (leader) {
-          issue_o(tO1, tS1, smem_addr(sV + pv * C::kTileBytes), nkb - 1 > 0);
-          umma_commit(&ctl.v_empty[pv]);
-          umma_commit(&ctl.o_full[1]);
-        }
-        __syncwarp();
+      const int pv = (nkb - 1) % C::kStagesV;
+      ok = issue_pv(1, smem_addr(sV + pv * C::kTileBytes), nkb - 1 > 0, (nkb - 1) & 1, kWatchP + 4);
+      if (ok && leader) {
+        umma_commit(&ctl.v_empty[pv]);
+        umma_commit(&ctl.o_full[1]);
       }
+      __syncwarp();
     }
     // Every UMMA this warp issued has retired before TMEM is released.
     if (leader) umma_commit(&ctl.mma_done);
@@ -289,84 +374,127 @@ __global__ void __launch_bounds__(320, 1)
     const uint32_t tS = tmem + lane_off + t * 128;
     const uint32_t tO = tmem + lane_off + C::kColO + t * kD;
     const float c = p.scale_log2;
+    const uint64_t c2 = f2(c, c);
     float m = -INFINITY;  // running max of raw scores (exp2 reference point)
     float l = 0.f;        // running sum of probabilities relative to m
     bool ok = true;
 
-    for (int j = 0; j < n_t; ++j) {
-      ok = __all_sync(0xffffffffu, mbar_wait(&ctl.s_full[t], j & 1, abort_flag, status, kWatchS + 1 + t));
-      if (!ok) break;
-      tc_fence_after();
-      float s[128];
-      {
-        uint32_t u0[32], u1[32], u2[32], u3[32];
-        tmem_ld32(tS + 0, u0);
-        tmem_ld32(tS + 32, u1);
-        tmem_ld32(tS + 64, u2);
-        tmem_ld32(tS + 96, u3);
-        tmem_wait_ld();
+    // Stores one 64-key half of P (over S columns [32h, 32h+32)) and signals it.
+    auto store_half = [&](int h, const uint32_t (&pk)[32]) {
+      tmem_st32(tS + 32 * h, pk);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&ctl.p_full[t][h]);
+    };
+
+    // Loads the 128 fp32 scores of this thread's row and masks keys past Lk
+    // and, when causal, keys after the query.
+    auto load_scores = [&](int j, float (&s)[128]) {
+      uint32_t u0[32], u1[32], u2[32], u3[32];
+      tmem_ld32(tS + 0, u0);
+      tmem_ld32(tS + 32, u1);
+      tmem_ld32(tS + 64, u2);
+      tmem_ld32(tS + 96, u3);
+      tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          s[i] = __uint_as_float(u0[i]);
-          s[32 + i] = __uint_as_float(u1[i]);
-          s[64 + i] = __uint_as_float(u2[i]);
-          s[96 + i] = __uint_as_float(u3[i]);
-        }
+      for (int i = 0; i < 32; ++i) {
+        s[i] = __uint_as_float(u0[i]);
+        s[32 + i] = __uint_as_float(u1[i]);
+        s[64 + i] = __uint_as_float(u2[i]);
+        s[96 + i] = __uint_as_float(u3[i]);
       }
       const int kbase = j * 128;
-      const bool need_mask = (kbase + 128 > p.Lk) || (kCausal && kbase + 127 > q0 + t * 128);
-      if (need_mask) {
+      if ((kbase + 128 > p.Lk) || (kCausal && kbase + 127 > q0 + t * 128)) {
         int limit = p.Lk - 1 - kbase;
         if (kCausal) limit = min(limit, row_abs - kbase);
 #pragma unroll
         for (int i = 0; i < 128; ++i)
           if (i > limit) s[i] = -INFINITY;
       }
-      float mx[8];
+    };
+
+    for (int j = 0; j < n_t; ++j) {
+      RA_MARK(t * 2048 + j * 16 + 0);
+      ok = __all_sync(0xffffffffu, mbar_wait(&ctl.s_full[t], j & 1, abort_flag, status, kWatchS + 1 + t));
+      if (!ok) break;
+      tc_fence_after();
+      RA_MARK(t * 2048 + j * 16 + 1);
+      float s[128];
+      load_scores(j, s);
+      RA_MARK(t * 2048 + j * 16 + 2);
+      // Row max of the block: four independent chains of 3-input max.
+      float mx[4] = {s[0], s[1], s[2], s[3]};
 #pragma unroll
-      for (int i = 0; i < 8; ++i) mx[i] = s[i];
-#pragma unroll
-      for (int i = 8; i < 128; ++i) mx[i & 7] = fmaxf(mx[i & 7], s[i]);
-      const float mb = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                             fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
-      const float m_new = fmaxf(m, mb);
-      const bool grow = (m_new - m) * c > 8.0f;
-      float alpha = 1.f;
-      if (grow) {
-        alpha = (m == -INFINITY) ? 0.f : ex2_approx((m - m_new) * c);
-        l *= alpha;
-        m = m_new;
+      for (int i = 4; i < 124; i += 8) {
+        mx[0] = fmax3(mx[0], s[i + 0], s[i + 4]);
+        mx[1] = fmax3(mx[1], s[i + 1], s[i + 5]);
+        mx[2] = fmax3(mx[2], s[i + 2], s[i + 6]);
+        mx[3] = fmax3(mx[3], s[i + 3], s[i + 7]);
       }
-      if (j > 0 && __any_sync(0xffffffffu, grow)) {
-        // Rare: bring O (all PV of earlier blocks have retired) onto the new max.
+      const float mb = fmax3(fmax3(mx[0], mx[1], s[124]), fmax3(mx[2], mx[3], s[125]), fmaxf(s[126], s[127]));
+
+      // Exponentials of the first half against the running max, computed
+      // while the block max is still being reduced: after the first blocks
+      // the max almost never moves by more than 2^8, and then these values
+      // are final.
+      uint64_t sum0 = f2(0.f, 0.f), sum1 = f2(0.f, 0.f);
+      uint32_t pk[32];
+      {
+        const float mc = (m == -INFINITY) ? 0.f : m * c;
+        const uint64_t nmc2 = f2(-mc, -mc);
+        exp_pack32<kBf16, 0, 0>(s, c2, nmc2, pk, sum0);
+        exp_pack32<kBf16, 32, 16>(s, c2, nmc2, pk, sum1);
+      }
+      RA_MARK(t * 2048 + j * 16 + 3);
+      const bool grow = (fmaxf(m, mb) - m) * c > 8.0f;
+      if (__any_sync(0xffffffffu, grow)) {
+        // The running max moves for some row of this warp (always on the first
+        // block).  Rows that grow take the block max; O and l are rescaled
+        // (S(j) retired, so every P*V product up to block j-1 has too) and
+        // the first half is recomputed from the scores, still intact in TMEM.
+        float alpha = 1.f;
+        if (grow) {
+          alpha = (m == -INFINITY) ? 0.f : ex2_approx((m - mb) * c);
+          l *= alpha;
+          m = mb;
+        }
+        if (j > 0) {
 #pragma unroll 1
-        for (int cc = 0; cc < kD; cc += 32) {
-          uint32_t o[32];
-          tmem_ld32(tO + cc, o);
-          tmem_wait_ld();
+          for (int cc = 0; cc < kD; cc += 32) {
+            uint32_t o[32];
+            tmem_ld32(tO + cc, o);
+            tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          tmem_st32(tO + cc, o);
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st32(tO + cc, o);
+          }
         }
+        load_scores(j, s);
+        const float mc = m * c;
+        const uint64_t nmc2 = f2(-mc, -mc);
+        sum0 = f2(0.f, 0.f);
+        sum1 = f2(0.f, 0.f);
+        exp_pack32<kBf16, 0, 0>(s, c2, nmc2, pk, sum0);
+        exp_pack32<kBf16, 32, 16>(s, c2, nmc2, pk, sum1);
       }
-      const float mc = (m == -INFINITY) ? 0.f : m * c;
-      float ls[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        uint32_t pk[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float a = ex2_approx(fmaf(s[64 * h + 2 * i], c, -mc));
-          const float b = ex2_approx(fmaf(s[64 * h + 2 * i + 1], c, -mc));
-          ls[i & 3] += a + b;
-          pk[i] = pack2<kBf16>(a, b);
-        }
-        tmem_st32(tS + 32 * h, pk);
+      RA_MARK(t * 2048 + j * 16 + 4);
+      store_half(0, pk);
+      RA_MARK(t * 2048 + j * 16 + 5);
+      {
+        const float mc = m * c;
+        const uint64_t nmc2 = f2(-mc, -mc);
+        exp_pack32<kBf16, 64, 0>(s, c2, nmc2, pk, sum0);
+        exp_pack32<kBf16, 96, 16>(s, c2, nmc2, pk, sum1);
       }
-      l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(&ctl.p_full[t]);
+      RA_MARK(t * 2048 + j * 16 + 6);
+      store_half(1, pk);
+      RA_MARK(t * 2048 + j * 16 + 7);
+      {
+        float a0, a1, b0, b1;
+        f2_split(sum0, a0, a1);
+        f2_split(sum1, b0, b1);
+        l += (a0 + a1) + (b0 + b1);
+      }
     }
 
     // ------------------------------------------------------------- epilogue
@@ -393,7 +521,7 @@ __global__ void __launch_bounds__(320, 1)
           v.z = pack2<kBf16>(__uint_as_float(o[8 * q4 + 4]) * inv_l, __uint_as_float(o[8 * q4 + 5]) * inv_l);
           v.w = pack2<kBf16>(__uint_as_float(o[8 * q4 + 6]) * inv_l, __uint_as_float(o[8 * q4 + 7]) * inv_l);
           const int chunk = chunk0 + q4;
-          const uint32_t off = cb * 16384 + row_in_tile * 128 + ((chunk ^ (row_in_tile & 7)) << 4);
+          const uint32_t off = cb * C::kBlockBytes + row_in_tile * 128 + ((chunk ^ (row_in_tile & 7)) << 4);
           *reinterpret_cast<uint4*>(stage + off) = v;
         }
       }
@@ -403,12 +531,13 @@ __global__ void __launch_bounds__(320, 1)
     named_barrier_sync(1 + t, 128);
     if (store && (threadIdx.x & 127) == 0) {
       for (int cb = 0; cb < kD / 64; ++cb)
-        tma_store_3d(&map_o, smem_addr(stage + cb * 16384), cb * 64, q0 + t * 128, bh);
+        tma_store_3d(&map_o, smem_addr(stage + cb * C::kBlockBytes), cb * 64, q0 + t * 128, bh);
       tma_store_commit();
       tma_store_wait_all();
     }
   }
 
+  RA_MARK(8180 - warp);
   tc_fence_before();
   __syncthreads();
   if (warp == 8) {
@@ -453,6 +582,9 @@ static int launch_impl(const void* q, const void* k, const void* v, void* out, i
   prm.Lk = Skv;
   prm.BH = BH;
   prm.num_qblocks = (Sq + 255) / 256;
+  // K+V bytes of one head; about 48 MB of them (a third of L2) per group.
+  const double kv_bytes = 2.0 * Skv * kD * 2;
+  prm.head_group = static_cast<int>(fmax(1.0, fmin(static_cast<double>(BH), 48.0e6 / kv_bytes)));
   prm.scale_log2 = scale * 1.4426950408889634f;
   const long long grid = static_cast<long long>(prm.num_qblocks) * BH;
   if (grid > 0x7fffffffLL) return ATTN_ERR_INVALID_ARGUMENT;
@@ -532,3 +664,19 @@ extern "C" int attn_get_status(cudaStream_t stream, int* status) {
 }
 
 extern "C" int attn_library_version(void) { return 100; }
+
+#ifdef RA_TRACE
+// Trace builds only: selects the traced CTA and copies the timeline out.
+extern "C" ATTN_API int attn_trace_read(int next_cta, unsigned long long* host, int n) {
+  if (cudaDeviceSynchronize() != cudaSuccess) return ATTN_ERR_LAUNCH;
+  if (host && n > 0 &&
+      cudaMemcpyFromSymbol(host, ra::g_attn_trace, sizeof(unsigned long long) * (n < ra::kTraceSlots ? n : ra::kTraceSlots)) !=
+          cudaSuccess)
+    return ATTN_ERR_LAUNCH;
+  static unsigned long long zeros[ra::kTraceSlots];
+  if (cudaMemcpyToSymbol(ra::g_attn_trace, zeros, sizeof(zeros)) != cudaSuccess ||
+      cudaMemcpyToSymbol(ra::g_attn_trace_cta, &next_cta, sizeof(int)) != cudaSuccess)
+    return ATTN_ERR_LAUNCH;
+  return ATTN_OK;
+}
+#endif

@@ -290,6 +290,64 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Packed pairs of fp32 (one 64-bit register pair) and the sm_100 f32x2 ALU
+// forms: one instruction does two lanes' worth of FMA/ADD.
+__device__ __forceinline__ uint64_t f2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_split(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
+// 2^x for a pair of inputs on the FMA/ALU pipes instead of the MUFU.
+// Method: round-to-nearest range reduction x = j + f, f in [-1/2, 1/2], via
+// the 1.5*2^23 addition trick (the integer j lands in the low mantissa bits
+// of t = x + 1.5*2^23); 2^f from a degree-3 polynomial whose coefficients
+// minimise the maximum relative error on [-1/2, 1/2] (fitted for this file
+// by linear programming on a 4001-point grid; max relative error 7.5e-5,
+// below the 2.4e-4 half-ulp of fp16); then 2^j is applied by adding j << 23
+// to the bit pattern of 2^f.  Inputs are clamped to >= -126 so the exponent
+// never wraps; such inputs return ~2^-126 instead of 0, which rounds to 0 in
+// fp16 and is negligible in bf16 and in the fp32 row sum.
+__device__ __forceinline__ void exp2_poly2(float x0, float x1, float& y0, float& y1) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  constexpr float c0 = 0x1.fff692p-1f, c1 = 0x1.62f31ap-1f, c2 = 0x1.f0de1ap-3f, c3 = 0x1.c3f760p-5f;
+  const uint64_t x = f2(fmaxf(x0, -126.f), fmaxf(x1, -126.f));
+  const uint64_t t = f2_add(x, f2(kRound, kRound));
+  const uint64_t f = f2_sub(x, f2_sub(t, f2(kRound, kRound)));
+  uint64_t p = f2_fma(f2(c3, c3), f, f2(c2, c2));
+  p = f2_fma(p, f, f2(c1, c1));
+  p = f2_fma(p, f, f2(c0, c0));
+  float p0, p1, t0, t1;
+  f2_split(p, p0, p1);
+  f2_split(t, t0, t1);
+  y0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
+  y1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
+}
+
 template <bool kBf16>
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   if constexpr (kBf16) {
