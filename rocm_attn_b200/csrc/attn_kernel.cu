@@ -81,7 +81,12 @@ struct Cfg {
   static constexpr uint32_t kBlockBytes = 128u * 128;   // one 64-column block of a tile
   static constexpr uint32_t kSmemBytes = 1024 + 2 * kTileBytes + (kStagesK + kStagesV) * kTileBytes;
   static constexpr uint32_t kTmemCols = 512;
-  static constexpr uint32_t kColO = 256;
+  // D=64 leaves TMEM room for P apart from S: the scores of block j+1 can
+  // then be computed while the softmax of block j is still running.  At
+  // D=128, P aliases the first half of S.
+  static constexpr bool kSepP = kD == 64;
+  static constexpr uint32_t kColP = 256;                  // P0, P1 (64 columns each) when kSepP
+  static constexpr uint32_t kColO = kSepP ? 384 : 256;    // O0, O1
   static constexpr int kThreads = 320;
 };
 
@@ -101,6 +106,8 @@ struct __align__(8) SharedCtl {
   uint64_t k_full[3], k_empty[3];
   uint64_t v_full[3], v_empty[3];
   uint64_t s_full[2];     // [tile]: S(j) computed
+  uint64_t s_free[2];     // [tile]: softmax done reading S(j) (128 arrivals; separate-P layout)
+  uint64_t p_free[2];     // [tile]: one phase per retired P*V product (separate-P layout)
   uint64_t p_full[2][2];  // [tile][64-key half]: P(j) half stored (128 arrivals)
   uint64_t o_full[2];     // [tile]: the last P*V product retired
   uint64_t mma_done;
@@ -191,6 +198,8 @@ __global__ void __launch_bounds__(320, 1)
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&ctl.s_full[t], 1);
+      mbar_init(&ctl.s_free[t], 128);
+      mbar_init(&ctl.p_free[t], 1);
       mbar_init(&ctl.p_full[t][0], 128);
       mbar_init(&ctl.p_full[t][1], 128);
       mbar_init(&ctl.o_full[t], 1);
@@ -287,7 +296,7 @@ __global__ void __launch_bounds__(320, 1)
     // the product overlaps the softmax of the second half.
     auto issue_pv = [&](int t, uint32_t v_addr, bool acc, uint32_t parity, int code) -> bool {
       const uint32_t d_tmem = t == 0 ? tO0 : tO1;
-      const uint32_t p_tmem = t == 0 ? tS0 : tS1;
+      const uint32_t p_tmem = C::kSepP ? tmem + C::kColP + t * 64 : (t == 0 ? tS0 : tS1);
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         if (!__all_sync(0xffffffffu, mbar_wait(&ctl.p_full[t][h], parity, abort_flag, status, code + h)))
@@ -305,6 +314,65 @@ __global__ void __launch_bounds__(320, 1)
     };
 
     bool ok = __all_sync(0xffffffffu, mbar_wait(&ctl.q_full, 0, abort_flag, status, kWatchQ + 2));
+    if constexpr (C::kSepP) {
+      // Issue order: S0(0) S1(0) | per block j: S0(j+1) O0+=P0(j)V(j) S1(j+1) O1+=P1(j)V(j).
+      // S(j+1) only waits for the softmax to have read S(j) (s_free), so the
+      // scores of the next block are ready when the softmax finishes.
+      const int nt[2] = {n0, n1};
+      if (ok) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&ctl.k_full[0], 0, abort_flag, status, kWatchK + 2));
+        if (ok) {
+          tc_fence_after();
+          if (leader) {
+            if (n0 > 0) { issue_s(tS0, q_addr0, smem_addr(sK)); umma_commit(&ctl.s_full[0]); }
+            if (n1 > 0) { issue_s(tS1, q_addr1, smem_addr(sK)); umma_commit(&ctl.s_full[1]); }
+            umma_commit(&ctl.k_empty[0]);
+          }
+          __syncwarp();
+        }
+      }
+      for (int j = 0; j < nkb && ok; ++j) {
+        RA_MARK(4096 + j * 8 + 0);
+        const int sk1 = (j + 1) % C::kStagesK, sv = j % C::kStagesV;
+        if (j + 1 < nkb) {
+          ok = __all_sync(0xffffffffu, mbar_wait(&ctl.k_full[sk1], ((j + 1) / C::kStagesK) & 1, abort_flag,
+                                                 status, kWatchK + 3));
+          if (!ok) break;
+        }
+        ok = __all_sync(0xffffffffu,
+                        mbar_wait(&ctl.v_full[sv], (j / C::kStagesV) & 1, abort_flag, status, kWatchV + 2));
+        if (!ok) break;
+        for (int t = 0; t < 2 && ok; ++t) {
+          if (j + 1 < nt[t]) {
+            ok = __all_sync(0xffffffffu, mbar_wait(&ctl.s_free[t], j & 1, abort_flag, status, kWatchS + 5 + t));
+            if (!ok) break;
+            tc_fence_after();
+            if (leader) {
+              issue_s(t == 0 ? tS0 : tS1, t == 0 ? q_addr0 : q_addr1, smem_addr(sK + sk1 * C::kTileBytes));
+              umma_commit(&ctl.s_full[t]);
+            }
+            __syncwarp();
+          }
+          if (j < nt[t]) {
+            ok = issue_pv(t, smem_addr(sV + sv * C::kTileBytes), j > 0, j & 1, kWatchP + 2 * t);
+            if (!ok) break;
+            if (leader) {
+              umma_commit(&ctl.p_free[t]);
+              if (j == nt[t] - 1) umma_commit(&ctl.o_full[t]);
+            }
+            __syncwarp();
+          }
+        }
+        if (!ok) break;
+        if (leader) {
+          if (j + 1 < nkb) umma_commit(&ctl.k_empty[sk1]);
+          umma_commit(&ctl.v_empty[sv]);
+        }
+        __syncwarp();
+        RA_MARK(4096 + j * 8 + 1);
+      }
+    } else {
+    // Issue order per key block j: S0(j), O1 += P1(j-1) V(j-1), S1(j), O0 += P0(j) V(j).
     // Issue order per key block j: S0(j), O1 += P1(j-1) V(j-1), S1(j), O0 += P0(j) V(j).
     for (int j = 0; j < nkb && ok; ++j) {
       const int sk = j % C::kStagesK, sv = j % C::kStagesV;
@@ -359,6 +427,7 @@ __global__ void __launch_bounds__(320, 1)
       }
       __syncwarp();
     }
+    }
     // Every UMMA this warp issued has retired before TMEM is released.
     if (leader) umma_commit(&ctl.mma_done);
     __syncwarp();
@@ -372,6 +441,7 @@ __global__ void __launch_bounds__(320, 1)
     const int n_t = t == 0 ? n0 : n1;
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t tS = tmem + lane_off + t * 128;
+    const uint32_t tP = C::kSepP ? tmem + lane_off + C::kColP + t * 64 : tS;
     const uint32_t tO = tmem + lane_off + C::kColO + t * kD;
     const float c = p.scale_log2;
     const uint64_t c2 = f2(c, c);
@@ -379,9 +449,9 @@ __global__ void __launch_bounds__(320, 1)
     float l = 0.f;        // running sum of probabilities relative to m
     bool ok = true;
 
-    // Stores one 64-key half of P (over S columns [32h, 32h+32)) and signals it.
+    // Stores one 64-key half of P (P columns [32h, 32h+32)) and signals it.
     auto store_half = [&](int h, const uint32_t (&pk)[32]) {
-      tmem_st32(tS + 32 * h, pk);
+      tmem_st32(tP + 32 * h, pk);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&ctl.p_full[t][h]);
@@ -458,6 +528,13 @@ __global__ void __launch_bounds__(320, 1)
           l *= alpha;
           m = mb;
         }
+        if (C::kSepP && j > 0) {
+          // Separate-P layout: S(j) may retire before the product of block
+          // j-1, so wait for that product before touching O.
+          ok = __all_sync(0xffffffffu, mbar_wait(&ctl.p_free[t], (j - 1) & 1, abort_flag, status, kWatchO + 5 + t));
+          if (!ok) break;
+          tc_fence_after();
+        }
         if (j > 0) {
 #pragma unroll 1
           for (int cc = 0; cc < kD; cc += 32) {
@@ -478,6 +555,18 @@ __global__ void __launch_bounds__(320, 1)
         exp_pack32<kBf16, 32, 16>(s, c2, nmc2, pk, sum1);
       }
       RA_MARK(t * 2048 + j * 16 + 4);
+      if constexpr (C::kSepP) {
+        // Every score of this block is in registers now (the first half
+        // already as packed P): let the next block's S*K^T overwrite S, and
+        // store P only once the previous block's product has read it.
+        tc_fence_before();
+        mbar_arrive(&ctl.s_free[t]);
+        if (j > 0) {
+          ok = __all_sync(0xffffffffu, mbar_wait(&ctl.p_free[t], (j - 1) & 1, abort_flag, status, kWatchO + 5 + t));
+          if (!ok) break;
+          tc_fence_after();
+        }
+      }
       store_half(0, pk);
       RA_MARK(t * 2048 + j * 16 + 5);
       {
