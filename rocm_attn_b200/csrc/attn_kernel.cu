@@ -206,6 +206,22 @@ __global__ void __launch_bounds__(320, 1)
     }
     mbar_init(&ctl.mma_done, 1);
     fence_mbar_init();
+    // Start the first copies (Q tiles, K and V of block 0) before the CTA
+    // synchronises and allocates tensor memory; the producer warp issues
+    // every later block.
+    const uint64_t pol_stream = l2_policy_evict_first();
+    const uint64_t pol_keep = l2_policy_evict_last();
+    mbar_arrive_expect_tx(&ctl.q_full, (n1 > 0 ? 2u : 1u) * C::kTileBytes);
+    for (int t = 0; t < (n1 > 0 ? 2 : 1); ++t)
+      for (int cb = 0; cb < kD / 64; ++cb)
+        tma_load_3d(smem_addr(sQ + t * C::kTileBytes + cb * C::kBlockBytes), &map_q, &ctl.q_full, cb * 64,
+                    q0 + t * 128, bh, pol_stream);
+    mbar_arrive_expect_tx(&ctl.k_full[0], C::kTileBytes);
+    for (int cb = 0; cb < kD / 64; ++cb)
+      tma_load_3d(smem_addr(sK + cb * C::kBlockBytes), &map_k, &ctl.k_full[0], cb * 64, 0, bh, pol_keep);
+    mbar_arrive_expect_tx(&ctl.v_full[0], C::kTileBytes);
+    for (int cb = 0; cb < kD / 64; ++cb)
+      tma_load_3d(smem_addr(sV + cb * C::kBlockBytes), &map_v, &ctl.v_full[0], cb * 64, 0, bh, pol_keep);
   }
   if (warp == 8) {
     tmem_alloc(smem_addr(&ctl.tmem_base), C::kTmemCols);
@@ -225,19 +241,11 @@ __global__ void __launch_bounds__(320, 1)
   RA_MARK(8190 - warp);
   if (warp == 9) {
     // ------------------------------------------------------------------ TMA
-    const uint64_t pol_stream = l2_policy_evict_first();
     const uint64_t pol_keep = l2_policy_evict_last();
     const bool leader = elect_one();
-    int last_k[3] = {-1, -1, -1}, last_v[3] = {-1, -1, -1};
-    if (leader) {
-      mbar_arrive_expect_tx(&ctl.q_full, (n1 > 0 ? 2u : 1u) * C::kTileBytes);
-      for (int t = 0; t < (n1 > 0 ? 2 : 1); ++t)
-        for (int cb = 0; cb < kD / 64; ++cb)
-          tma_load_3d(smem_addr(sQ + t * C::kTileBytes + cb * C::kBlockBytes), &map_q, &ctl.q_full, cb * 64,
-                      q0 + t * 128, bh, pol_stream);
-    }
+    int last_k[3] = {0, -1, -1}, last_v[3] = {0, -1, -1};  // block 0 was issued during setup
     bool ok = true;
-    for (int j = 0; j < nkb && ok; ++j) {
+    for (int j = 1; j < nkb && ok; ++j) {
       const int sk = j % C::kStagesK;
       RA_MARK(6144 + j * 4 + 0);
       ok = __all_sync(0xffffffffu,
@@ -622,7 +630,7 @@ __global__ void __launch_bounds__(320, 1)
       for (int cb = 0; cb < kD / 64; ++cb)
         tma_store_3d(&map_o, smem_addr(stage + cb * C::kBlockBytes), cb * 64, q0 + t * 128, bh);
       tma_store_commit();
-      tma_store_wait_all();
+      tma_store_wait_smem_read();
     }
   }
 

@@ -131,6 +131,13 @@ __device__ __forceinline__ void tma_store_commit() { asm volatile("cp.async.bulk
 
 __device__ __forceinline__ void tma_store_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
+// Waits until every committed bulk store has finished reading its shared
+// memory source (the global writes may still be in flight; they are complete
+// and visible when the kernel ends).
+__device__ __forceinline__ void tma_store_wait_smem_read() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
 // Makes generic-proxy shared-memory writes visible to the async (TMA) proxy.
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
