@@ -36,18 +36,24 @@ def _load_ext():
 
 rocm_attn_ext = _load_ext()
 
+# Head dims and dtypes of the tcgen05 tensor-core kernel; every other call
+# with 1 <= D <= MAX_HEAD_DIM (and fp32 at any such D) runs the general
+# fp32-arithmetic kernel.
 SUPPORTED_HEAD_DIMS = (64, 128)
 SUPPORTED_DTYPES = (torch.float16, torch.bfloat16)
+MAX_HEAD_DIM = 256
 
 
 def attn_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = False,
                  scale: Optional[float] = None) -> torch.Tensor:
     """Scaled dot-product attention forward.
 
-    q: [B, H, Lq, D], k/v: [B, H, Lk, D], fp16 or bf16 CUDA tensors, D in
-    {64, 128}.  ``causal`` masks key j for query i when j > i (top-left
-    aligned, as torch SDPA ``is_causal=True``).  ``scale`` defaults to
-    1/sqrt(D).  Returns O [B, H, Lq, D] in q's dtype.
+    q: [B, H, Lq, D], k/v: [B, H, Lk, D], fp16, bf16 or fp32 CUDA tensors,
+    1 <= D <= 256.  fp16/bf16 with D in {64, 128} run the tcgen05
+    tensor-core kernel; other calls run the general kernel (fp32 math).
+    ``causal`` masks key j for query i when j > i (top-left aligned, as torch
+    SDPA ``is_causal=True``).  ``scale`` defaults to 1/sqrt(D).  Returns O
+    [B, H, Lq, D] in q's dtype.
     """
     return rocm_attn_ext.attn_forward(q, k, v, bool(causal), -1.0 if scale is None else float(scale))
 
@@ -60,4 +66,4 @@ def check_status(device: int = 0) -> int:
 
 
 __all__ = ["attn_forward", "check_status", "rocm_attn_ext", "KERNEL_LIB_PATH",
-           "SUPPORTED_HEAD_DIMS", "SUPPORTED_DTYPES"]
+           "SUPPORTED_HEAD_DIMS", "SUPPORTED_DTYPES", "MAX_HEAD_DIM"]

@@ -1,7 +1,9 @@
 """In-tree build of the native parts.
 
 * ``librocm_attn.so``  -- the sm_100a kernels and the C-ABI launcher
-  (``csrc/attn_kernel.cu``), compiled by nvcc for ``sm_100a`` only, with the
+  (``csrc/attn_kernel.cu``: tensor-core kernel and dispatch;
+  ``csrc/attn_general.cu``: fp32 / other head dims), compiled by nvcc for
+  ``sm_100a`` only, with the
   CUDA runtime linked statically so the library loads without torch.
 * ``rocm_attn_ext*.so`` -- the PyTorch binding (``csrc/attn_torch.cpp``),
   linked against ``librocm_attn.so`` through an ``$ORIGIN`` rpath.
@@ -51,11 +53,11 @@ def _kernel_sources() -> list[str]:
 
 
 def build_kernel_lib(force: bool = False, verbose: bool = False) -> str:
-    """Compile csrc/attn_kernel.cu into librocm_attn.so (sm_100a)."""
+    """Compile csrc/*.cu into librocm_attn.so (sm_100a)."""
     if not force and not _newer(KERNEL_LIB, _kernel_sources()):
         return KERNEL_LIB
     cmd = [_nvcc(), *NVCC_FLAGS, "-I", INCLUDE, "-shared",
-           os.path.join(CSRC, "attn_kernel.cu"), "-o", KERNEL_LIB + ".tmp"]
+           os.path.join(CSRC, "attn_kernel.cu"), os.path.join(CSRC, "attn_general.cu"), "-o", KERNEL_LIB + ".tmp"]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
     subprocess.run(cmd, check=True)

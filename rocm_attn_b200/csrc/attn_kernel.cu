@@ -30,6 +30,7 @@
 #include "sm100_ptx.cuh"
 #include "tensor_map.h"
 #include "attn_kernel.h"
+#include "attn_general.h"
 
 #include <math.h>
 #include <mutex>
@@ -711,27 +712,36 @@ extern "C" int launch_attn_forward(const void* q, const void* k, const void* v, 
                                    cudaStream_t stream) {
   using namespace ra;
   if (B < 0 || H < 0 || Sq < 0 || Skv < 0 || D <= 0) return ATTN_ERR_INVALID_ARGUMENT;
-  if (dtype != ATTN_F16 && dtype != ATTN_BF16) return ATTN_ERR_UNSUPPORTED;
-  if (D != 64 && D != 128) return ATTN_ERR_UNSUPPORTED;
+  if (dtype != ATTN_F16 && dtype != ATTN_BF16 && dtype != ATTN_F32) return ATTN_ERR_UNSUPPORTED;
+  if (D > kGeneralMaxHeadDim) return ATTN_ERR_UNSUPPORTED;
   const long long BH = static_cast<long long>(B) * H;
   if (BH == 0 || Sq == 0) return ATTN_OK;  // empty output, nothing to do
   if (BH > 0x7fffffffLL) return ATTN_ERR_INVALID_ARGUMENT;
   if (!q || !out || (Skv > 0 && (!k || !v))) return ATTN_ERR_INVALID_ARGUMENT;
-  auto misaligned = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) != 0; };
-  if (misaligned(q) || misaligned(out) || (Skv > 0 && (misaligned(k) || misaligned(v))))
+  const size_t elem = dtype == ATTN_F32 ? 4 : 2;
+  auto aligned = [](const void* ptr, size_t a) { return (reinterpret_cast<uintptr_t>(ptr) & (a - 1)) == 0; };
+  if (!aligned(q, elem) || !aligned(out, elem) || (Skv > 0 && (!aligned(k, elem) || !aligned(v, elem))))
     return ATTN_ERR_MISALIGNED;
   const int dev_ok = check_device();
   if (dev_ok != ATTN_OK) return dev_ok;
   if (Skv == 0) {
     // No keys: every row's softmax denominator is empty; the reference
     // writes zeros in that case.
-    const size_t bytes = static_cast<size_t>(BH) * Sq * D * 2;
+    const size_t bytes = static_cast<size_t>(BH) * Sq * D * elem;
     return cudaMemsetAsync(out, 0, bytes, stream) == cudaSuccess ? ATTN_OK : ATTN_ERR_LAUNCH;
   }
   float scale = softmax_scale;
   if (!(scale > 0.f) || !isfinite(scale)) scale = 1.0f / sqrtf(static_cast<float>(D));
-  const bool bf16 = dtype == ATTN_BF16;
   const int bh = static_cast<int>(BH);
+  // The tensor-core kernel takes fp16/bf16 with D in {64, 128} and TMA-ready
+  // (16-byte aligned) buffers; every other call runs the general kernel.
+  const bool tensor_path = dtype != ATTN_F32 && (D == 64 || D == 128) && aligned(q, 16) && aligned(out, 16) &&
+                           aligned(k, 16) && aligned(v, 16);
+  if (!tensor_path)
+    return launch_attn_general(q, k, v, out, bh, Sq, Skv, D, causal, scale, static_cast<int>(dtype), stream) == 0
+               ? ATTN_OK
+               : ATTN_ERR_LAUNCH;
+  const bool bf16 = dtype == ATTN_BF16;
 #define RA_DISPATCH(BF, DD, CA) \
   if (bf16 == BF && D == DD && causal == CA) return launch_impl<BF, DD, CA>(q, k, v, out, bh, Sq, Skv, scale, stream);
   RA_DISPATCH(false, 128, false)

@@ -19,8 +19,8 @@ static const char* status_text(int s) {
   switch (s) {
     case ATTN_OK: return "ok";
     case ATTN_ERR_INVALID_ARGUMENT: return "invalid argument";
-    case ATTN_ERR_UNSUPPORTED: return "unsupported dtype or head_dim (supported: float16/bfloat16, D in {64, 128})";
-    case ATTN_ERR_MISALIGNED: return "q/k/v/out must be 16-byte aligned";
+    case ATTN_ERR_UNSUPPORTED: return "unsupported dtype or head_dim (supported: float16/bfloat16/float32, 1 <= D <= 256)";
+    case ATTN_ERR_MISALIGNED: return "q/k/v/out must be aligned to their element size";
     case ATTN_ERR_TENSOR_MAP: return "could not encode a TMA tensor map";
     case ATTN_ERR_LAUNCH: return "CUDA launch failed";
     case ATTN_ERR_DEVICE: return "the current device is not an sm_100 (B200-class) GPU";

@@ -62,16 +62,19 @@ def _call(lib, q=0x1000, k=0x1000, v=0x1000, o=0x1000, B=1, H=1, Sq=8, Skv=8, D=
 
 
 def test_argument_checks_before_any_cuda_call(lib):
-    assert _call(lib, D=96) == ATTN_ERR_UNSUPPORTED
-    assert _call(lib, D=16) == ATTN_ERR_UNSUPPORTED
-    assert _call(lib, dtype=2) == ATTN_ERR_UNSUPPORTED          # fp32 not built for sm_100a
+    # Every call here fails (or finishes) before the device is touched; the
+    # pointers are fake.
+    assert _call(lib, D=257) == ATTN_ERR_UNSUPPORTED            # general kernel takes D <= 256
+    assert _call(lib, D=1000) == ATTN_ERR_UNSUPPORTED
     assert _call(lib, dtype=7) == ATTN_ERR_UNSUPPORTED
+    assert _call(lib, D=0) == ATTN_ERR_INVALID_ARGUMENT
     assert _call(lib, B=-1) == ATTN_ERR_INVALID_ARGUMENT
     assert _call(lib, Sq=-3) == ATTN_ERR_INVALID_ARGUMENT
     assert _call(lib, q=None) == ATTN_ERR_INVALID_ARGUMENT
     assert _call(lib, o=None) == ATTN_ERR_INVALID_ARGUMENT
-    assert _call(lib, q=0x1008) == ATTN_ERR_MISALIGNED          # TMA needs 16-byte aligned bases
-    assert _call(lib, v=0x1004) == ATTN_ERR_MISALIGNED
+    assert _call(lib, q=0x1001) == ATTN_ERR_MISALIGNED          # not aligned to the 2-byte element
+    assert _call(lib, v=0x1003, dtype=1) == ATTN_ERR_MISALIGNED
+    assert _call(lib, k=0x1002, dtype=2) == ATTN_ERR_MISALIGNED  # fp32 needs 4-byte alignment
     # empty problems are a successful no-op
     assert _call(lib, B=0) == ATTN_OK
     assert _call(lib, Sq=0) == ATTN_OK

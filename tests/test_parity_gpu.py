@@ -172,11 +172,11 @@ def test_many_heads_tiny_sequences(attn):
 
 
 def test_rejects_unsupported(attn):
-    x = torch.randn(1, 1, 8, 96, device="cuda").half()
+    x = torch.randn(1, 1, 8, 264, device="cuda").half()
     with pytest.raises(RuntimeError, match="unsupported"):
         attn.attn_forward(x, x, x)
-    y = torch.randn(1, 1, 8, 64, device="cuda")
-    with pytest.raises(RuntimeError, match="unsupported"):
+    y = torch.randn(1, 1, 8, 64, device="cuda", dtype=torch.float64)
+    with pytest.raises(RuntimeError, match="float32, float16, or bfloat16"):
         attn.attn_forward(y, y, y)
     with pytest.raises(RuntimeError, match="CUDA"):
         attn.attn_forward(y.cpu(), y.cpu(), y.cpu())
