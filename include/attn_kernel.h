@@ -43,8 +43,8 @@ typedef enum AttnDType {
 enum AttnStatus {
   ATTN_OK = 0,
   ATTN_ERR_INVALID_ARGUMENT = 1, /* null pointer, negative size, overflow   */
-  ATTN_ERR_UNSUPPORTED = 2,      /* dtype / head_dim not built              */
-  ATTN_ERR_MISALIGNED = 3,       /* pointer not 16-byte aligned             */
+  ATTN_ERR_UNSUPPORTED = 2,      /* unknown dtype or head_dim > 256         */
+  ATTN_ERR_MISALIGNED = 3,       /* pointer not aligned to its element size */
   ATTN_ERR_TENSOR_MAP = 4,       /* TMA descriptor could not be encoded     */
   ATTN_ERR_LAUNCH = 5,           /* CUDA runtime error at launch            */
   ATTN_ERR_DEVICE = 6,           /* current device is not an sm_100 GPU     */
@@ -60,16 +60,36 @@ enum AttnStatus {
  * reference's rule at src/attn_kernel_torch.cu:54,238,263).  Skv == 0 gives
  * an all-zero output, like the reference's empty-denominator rule
  * (src/attn_kernel_torch.cu:335-336).
- * Supported: dtype ATTN_F16 / ATTN_BF16, D in {64, 128}; all pointers 16-byte
- * aligned.  Asynchronous on `stream`; allocates nothing; re-entrant.
+ * Supported: dtype ATTN_F16 / ATTN_BF16 / ATTN_F32 and 1 <= D <= 256, every
+ * pointer aligned to its element size.  fp16/bf16 with D in {64, 128} and
+ * 16-byte aligned buffers run the tcgen05 tensor-core kernel; every other
+ * supported call runs the general kernel (fp32 arithmetic), which covers the
+ * reference's fp32 and D=16 routes (src/attn_kernel_torch.cu:625-689).
+ * Asynchronous on `stream`; allocates nothing; re-entrant.
  * Returns ATTN_OK or an AttnStatus code; on error nothing was launched.
  */
 ATTN_API int launch_attn_forward(const void* q, const void* k, const void* v, void* out, int B, int H, int Sq, int Skv,
                         int D, bool causal, float softmax_scale, AttnDType dtype, cudaStream_t stream);
 
 /*
+ * launch_attn_forward on strided q, k and v: each *_strides array holds the
+ * element strides over (batch, head, row), the head dim being contiguous; a
+ * null array means the contiguous layout.  For example the [B, L, H, D]
+ * layout of flash-style callers viewed as [B, H, L, D] has strides
+ * {L*H*D, D, H*D}.  out stays contiguous [B, H, Sq, D].  The tensor-core
+ * kernel reads strided inputs directly through TMA when every stride is a
+ * multiple of 16 bytes; otherwise the general kernel runs.  Strides must be
+ * >= 0.  No counterpart in the reference, whose binding copies inputs to
+ * contiguous tensors first (src/attn_torch.cpp:20-22).
+ */
+ATTN_API int launch_attn_forward_strided(const void* q, const void* k, const void* v, void* out, int B, int H,
+                                         int Sq, int Skv, int D, bool causal, float softmax_scale, AttnDType dtype,
+                                         const long long* q_strides, const long long* k_strides,
+                                         const long long* v_strides, cudaStream_t stream);
+
+/*
  * Reads and clears the device status word of the current device, after
- * synchronising `stream`.  *status receives ATTN_OK, or ATTN_WATCHDOG when a
+ * synchronising `stream`.  *status receives ATTN_OK, or ATTN_ERR_WATCHDOG when a
  * kernel launched earlier gave up on a wait (its output is then invalid).
  * No counterpart in the reference, whose launcher has no error reporting.
  * Returns ATTN_OK, or ATTN_ERR_LAUNCH if the synchronisation itself failed.

@@ -10,7 +10,8 @@
 // running fp32 max and sum (:269-298), O = P V / sum (:333-354), and a row
 // with no unmasked key gives 0 (:335-336).
 //
-// Layout: q [BH, Sq, D], k/v [BH, Skv, D], o [BH, Sq, D], contiguous.
+// Layout: q [B, H, Sq, D], k/v [B, H, Skv, D] with any (batch, head, row)
+// strides and a contiguous head dim; o [B, H, Sq, D] contiguous.
 // CTA: 64 query rows of one (batch, head) and 256 threads, four per row;
 // thread t4 of a row owns the dims d = t4 + 4 i, so the four threads of a row
 // read four consecutive shared-memory banks.  Keys are staged in blocks of 32
@@ -45,8 +46,9 @@ template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(flo
 // kDMax: a multiple of 4 with D <= kDMax; each thread holds kDMax / 4 dims.
 template <typename T, int kDMax, bool kCausal>
 __global__ void __launch_bounds__(kThreads) attn_general_kernel(const T* __restrict__ q, const T* __restrict__ k,
-                                                                const T* __restrict__ v, T* __restrict__ o, int Sq,
-                                                                int Skv, int D, float scale_log2) {
+                                                                const T* __restrict__ v, T* __restrict__ o, int H,
+                                                                int Sq, int Skv, int D, float scale_log2,
+                                                                const GeneralStrides st) {
   constexpr int kPer = kDMax / 4;
   constexpr int kKeys = kDMax > 128 ? 16 : 32;  // keys per staged block (static shared memory <= 33 KB)
   constexpr int kStride = kDMax + 1;            // padded row of a staged key
@@ -59,8 +61,10 @@ __global__ void __launch_bounds__(kThreads) attn_general_kernel(const T* __restr
   const int row = rb * kRows + static_cast<int>(threadIdx.x) / 4;
   const int t4 = threadIdx.x & 3;
   const bool live = row < Sq;
-  const size_t q_base = (static_cast<size_t>(bh) * Sq + (live ? row : 0)) * D;
-  const size_t kv_base = static_cast<size_t>(bh) * Skv * D;
+  const long long b = bh / H, h = bh - b * H;
+  const long long q_base = b * st.q[0] + h * st.q[1] + static_cast<long long>(live ? row : 0) * st.q[2];
+  const long long k_base = b * st.k[0] + h * st.k[1], v_base = b * st.v[0] + h * st.v[1];
+  const size_t o_base = (static_cast<size_t>(bh) * Sq + (live ? row : 0)) * D;
 
   float qr[kPer], acc[kPer];
 #pragma unroll
@@ -81,8 +85,8 @@ __global__ void __launch_bounds__(kThreads) attn_general_kernel(const T* __restr
       const int kk = e / kDMax, d = e - kk * kDMax;
       const int key = k0 + kk;
       const bool in = key < Skv && d < D;
-      sK[kk * kStride + d] = in ? to_f32(k[kv_base + static_cast<size_t>(key) * D + d]) : 0.f;
-      sV[kk * kStride + d] = in ? to_f32(v[kv_base + static_cast<size_t>(key) * D + d]) : 0.f;
+      sK[kk * kStride + d] = in ? to_f32(k[k_base + key * st.k[2] + d]) : 0.f;
+      sV[kk * kStride + d] = in ? to_f32(v[v_base + key * st.v[2] + d]) : 0.f;
     }
     __syncthreads();
 
@@ -121,48 +125,50 @@ __global__ void __launch_bounds__(kThreads) attn_general_kernel(const T* __restr
 #pragma unroll
     for (int i = 0; i < kPer; ++i) {
       const int d = t4 + 4 * i;
-      if (d < D) o[q_base + d] = from_f32<T>(acc[i] * inv);
+      if (d < D) o[o_base + d] = from_f32<T>(acc[i] * inv);
     }
   }
 }
 
 template <typename T, int kDMax>
-int launch_typed(const void* q, const void* k, const void* v, void* out, int BH, int Sq, int Skv, int D, bool causal,
-                 float scale_log2, cudaStream_t stream) {
+int launch_typed(const void* q, const void* k, const void* v, void* out, int BH, int H, int Sq, int Skv, int D,
+                 bool causal, float scale_log2, const GeneralStrides& st, cudaStream_t stream) {
   const long long blocks = static_cast<long long>((Sq + kRows - 1) / kRows) * BH;
   if (blocks > 0x7fffffffLL) return -1;
   const dim3 grid(static_cast<unsigned>(blocks));
   if (causal)
     attn_general_kernel<T, kDMax, true><<<grid, kThreads, 0, stream>>>(
-        static_cast<const T*>(q), static_cast<const T*>(k), static_cast<const T*>(v), static_cast<T*>(out), Sq, Skv,
-        D, scale_log2);
+        static_cast<const T*>(q), static_cast<const T*>(k), static_cast<const T*>(v), static_cast<T*>(out), H, Sq,
+        Skv, D, scale_log2, st);
   else
     attn_general_kernel<T, kDMax, false><<<grid, kThreads, 0, stream>>>(
-        static_cast<const T*>(q), static_cast<const T*>(k), static_cast<const T*>(v), static_cast<T*>(out), Sq, Skv,
-        D, scale_log2);
+        static_cast<const T*>(q), static_cast<const T*>(k), static_cast<const T*>(v), static_cast<T*>(out), H, Sq,
+        Skv, D, scale_log2, st);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
 template <typename T>
-int launch_dims(const void* q, const void* k, const void* v, void* out, int BH, int Sq, int Skv, int D, bool causal,
-                float scale_log2, cudaStream_t stream) {
-  if (D <= 16) return launch_typed<T, 16>(q, k, v, out, BH, Sq, Skv, D, causal, scale_log2, stream);
-  if (D <= 32) return launch_typed<T, 32>(q, k, v, out, BH, Sq, Skv, D, causal, scale_log2, stream);
-  if (D <= 64) return launch_typed<T, 64>(q, k, v, out, BH, Sq, Skv, D, causal, scale_log2, stream);
-  if (D <= 128) return launch_typed<T, 128>(q, k, v, out, BH, Sq, Skv, D, causal, scale_log2, stream);
-  return launch_typed<T, 256>(q, k, v, out, BH, Sq, Skv, D, causal, scale_log2, stream);
+int launch_dims(const void* q, const void* k, const void* v, void* out, int BH, int H, int Sq, int Skv, int D,
+                bool causal, float scale_log2, const GeneralStrides& st, cudaStream_t stream) {
+  if (D <= 16) return launch_typed<T, 16>(q, k, v, out, BH, H, Sq, Skv, D, causal, scale_log2, st, stream);
+  if (D <= 32) return launch_typed<T, 32>(q, k, v, out, BH, H, Sq, Skv, D, causal, scale_log2, st, stream);
+  if (D <= 64) return launch_typed<T, 64>(q, k, v, out, BH, H, Sq, Skv, D, causal, scale_log2, st, stream);
+  if (D <= 128) return launch_typed<T, 128>(q, k, v, out, BH, H, Sq, Skv, D, causal, scale_log2, st, stream);
+  return launch_typed<T, 256>(q, k, v, out, BH, H, Sq, Skv, D, causal, scale_log2, st, stream);
 }
 
 }  // namespace
 
-int launch_attn_general(const void* q, const void* k, const void* v, void* out, int BH, int Sq, int Skv, int D,
-                        bool causal, float scale, int dtype, cudaStream_t stream) {
-  if (BH <= 0 || Sq <= 0 || Skv <= 0 || D <= 0 || D > kGeneralMaxHeadDim) return -1;
+int launch_attn_general(const void* q, const void* k, const void* v, void* out, int B, int H, int Sq, int Skv,
+                        int D, bool causal, float scale, int dtype, const GeneralStrides& st, cudaStream_t stream) {
+  const long long BH = static_cast<long long>(B) * H;
+  if (B <= 0 || H <= 0 || BH > 0x7fffffffLL || Sq <= 0 || Skv <= 0 || D <= 0 || D > kGeneralMaxHeadDim) return -1;
+  const int bh = static_cast<int>(BH);
   const float scale_log2 = scale * 1.4426950408889634f;
   switch (dtype) {
-    case 0: return launch_dims<__half>(q, k, v, out, BH, Sq, Skv, D, causal, scale_log2, stream);
-    case 1: return launch_dims<__nv_bfloat16>(q, k, v, out, BH, Sq, Skv, D, causal, scale_log2, stream);
-    case 2: return launch_dims<float>(q, k, v, out, BH, Sq, Skv, D, causal, scale_log2, stream);
+    case 0: return launch_dims<__half>(q, k, v, out, bh, H, Sq, Skv, D, causal, scale_log2, st, stream);
+    case 1: return launch_dims<__nv_bfloat16>(q, k, v, out, bh, H, Sq, Skv, D, causal, scale_log2, st, stream);
+    case 2: return launch_dims<float>(q, k, v, out, bh, H, Sq, Skv, D, causal, scale_log2, st, stream);
     default: return -1;
   }
 }

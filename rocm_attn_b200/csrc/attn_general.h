@@ -9,11 +9,19 @@ namespace ra {
 // Largest head dimension the general kernel takes.
 constexpr int kGeneralMaxHeadDim = 256;
 
-// Attention forward on contiguous q [BH, Sq, D], k/v [BH, Skv, D] -> out
-// [BH, Sq, D] in dtype 0 = fp16, 1 = bf16, 2 = fp32 (AttnDType values), fp32
-// arithmetic, any 1 <= D <= kGeneralMaxHeadDim, Sq, Skv >= 1.  Returns 0 when
-// the launch was queued, -1 otherwise.
-int launch_attn_general(const void* q, const void* k, const void* v, void* out, int BH, int Sq, int Skv, int D,
-                        bool causal, float scale, int dtype, cudaStream_t stream);
+// Element strides of q, k and v over (batch, head, row); the head dim of each
+// is contiguous.
+struct GeneralStrides {
+  long long q[3], k[3], v[3];
+};
+
+// Attention forward on q [B, H, Sq, D], k/v [B, H, Skv, D] (strided as
+// given) -> out [B, H, Sq, D] contiguous, in dtype 0 = fp16, 1 = bf16,
+// 2 = fp32 (AttnDType values), fp32 arithmetic, any 1 <= D <=
+// kGeneralMaxHeadDim, Sq, Skv >= 1.  Returns 0 when the launch was queued,
+// -1 otherwise.
+int launch_attn_general(const void* q, const void* k, const void* v, void* out, int B, int H, int Sq, int Skv,
+                        int D, bool causal, float scale, int dtype, const GeneralStrides& strides,
+                        cudaStream_t stream);
 
 }  // namespace ra

@@ -66,6 +66,7 @@ struct AttnParams {
   int Lq;           // query rows per (batch, head)
   int Lk;           // key rows per (batch, head)
   int BH;           // batch * heads
+  int H;            // heads (TMA coordinates are (d, row, head, batch))
   int num_qblocks;  // ceil(Lq / 256)
   int head_group;   // causal: heads per scheduling group (their K/V fit in L2)
   float scale_log2; // softmax scale * log2(e)
@@ -183,6 +184,7 @@ __global__ void __launch_bounds__(320, 1)
     bh = blockIdx.x / p.num_qblocks;
     qb = p.num_qblocks - 1 - static_cast<int>(blockIdx.x % p.num_qblocks);
   }
+  const int hh = bh % p.H, bb = bh / p.H;  // TMA coordinates of the (batch, head) slice
   const int q0 = qb * 256;
   const int n0 = tile_key_blocks(q0, 0, p.Lq, p.Lk, kCausal);
   const int n1 = tile_key_blocks(q0, 1, p.Lq, p.Lk, kCausal);
@@ -215,14 +217,14 @@ __global__ void __launch_bounds__(320, 1)
     mbar_arrive_expect_tx(&ctl.q_full, (n1 > 0 ? 2u : 1u) * C::kTileBytes);
     for (int t = 0; t < (n1 > 0 ? 2 : 1); ++t)
       for (int cb = 0; cb < kD / 64; ++cb)
-        tma_load_3d(smem_addr(sQ + t * C::kTileBytes + cb * C::kBlockBytes), &map_q, &ctl.q_full, cb * 64,
-                    q0 + t * 128, bh, pol_stream);
+        tma_load_4d(smem_addr(sQ + t * C::kTileBytes + cb * C::kBlockBytes), &map_q, &ctl.q_full, cb * 64,
+                    q0 + t * 128, hh, bb, pol_stream);
     mbar_arrive_expect_tx(&ctl.k_full[0], C::kTileBytes);
     for (int cb = 0; cb < kD / 64; ++cb)
-      tma_load_3d(smem_addr(sK + cb * C::kBlockBytes), &map_k, &ctl.k_full[0], cb * 64, 0, bh, pol_keep);
+      tma_load_4d(smem_addr(sK + cb * C::kBlockBytes), &map_k, &ctl.k_full[0], cb * 64, 0, hh, bb, pol_keep);
     mbar_arrive_expect_tx(&ctl.v_full[0], C::kTileBytes);
     for (int cb = 0; cb < kD / 64; ++cb)
-      tma_load_3d(smem_addr(sV + cb * C::kBlockBytes), &map_v, &ctl.v_full[0], cb * 64, 0, bh, pol_keep);
+      tma_load_4d(smem_addr(sV + cb * C::kBlockBytes), &map_v, &ctl.v_full[0], cb * 64, 0, hh, bb, pol_keep);
   }
   if (warp == 8) {
     tmem_alloc(smem_addr(&ctl.tmem_base), C::kTmemCols);
@@ -255,8 +257,8 @@ __global__ void __launch_bounds__(320, 1)
       if (leader) {
         mbar_arrive_expect_tx(&ctl.k_full[sk], C::kTileBytes);
         for (int cb = 0; cb < kD / 64; ++cb)
-          tma_load_3d(smem_addr(sK + sk * C::kTileBytes + cb * C::kBlockBytes), &map_k, &ctl.k_full[sk], cb * 64,
-                      j * 128, bh, pol_keep);
+          tma_load_4d(smem_addr(sK + sk * C::kTileBytes + cb * C::kBlockBytes), &map_k, &ctl.k_full[sk], cb * 64,
+                      j * 128, hh, bb, pol_keep);
       }
       last_k[sk] = j;
       RA_MARK(6144 + j * 4 + 1);
@@ -267,8 +269,8 @@ __global__ void __launch_bounds__(320, 1)
       if (leader) {
         mbar_arrive_expect_tx(&ctl.v_full[sv], C::kTileBytes);
         for (int cb = 0; cb < kD / 64; ++cb)
-          tma_load_3d(smem_addr(sV + sv * C::kTileBytes + cb * C::kBlockBytes), &map_v, &ctl.v_full[sv], cb * 64,
-                      j * 128, bh, pol_keep);
+          tma_load_4d(smem_addr(sV + sv * C::kTileBytes + cb * C::kBlockBytes), &map_v, &ctl.v_full[sv], cb * 64,
+                      j * 128, hh, bb, pol_keep);
       }
       last_v[sv] = j;
       RA_MARK(6144 + j * 4 + 2);
@@ -629,7 +631,7 @@ __global__ void __launch_bounds__(320, 1)
     named_barrier_sync(1 + t, 128);
     if (store && (threadIdx.x & 127) == 0) {
       for (int cb = 0; cb < kD / 64; ++cb)
-        tma_store_3d(&map_o, smem_addr(stage + cb * C::kBlockBytes), cb * 64, q0 + t * 128, bh);
+        tma_store_4d(&map_o, smem_addr(stage + cb * C::kBlockBytes), cb * 64, q0 + t * 128, hh, bb);
       tma_store_commit();
       tma_store_wait_smem_read();
     }
@@ -648,17 +650,32 @@ __global__ void __launch_bounds__(320, 1)
 // Host side
 // --------------------------------------------------------------------------
 
+// Element strides of one input over (batch, head, row); the head dim is
+// contiguous.
+struct Strides {
+  long long b, h, l;
+};
+
+// Returned by launch_impl when a buffer or stride cannot be described to TMA
+// (the caller then runs the general kernel).
+constexpr int kNoTensorMap = -2;
+
 template <bool kBf16, int kD, bool kCausal>
-static int launch_impl(const void* q, const void* k, const void* v, void* out, int BH, int Sq, int Skv,
-                       float scale, cudaStream_t stream) {
+static int launch_impl(const void* q, const void* k, const void* v, void* out, int B, int H, int Sq, int Skv,
+                       const Strides& sq, const Strides& sk, const Strides& sv, float scale, cudaStream_t stream) {
   using C = Cfg<kD>;
   CUtensorMap mq, mk, mv, mo;
   const uint64_t D = kD;
-  if (make_tensor_map_3d(&mq, q, kBf16, D, Sq, BH, D, static_cast<uint64_t>(Sq) * D, 64, 128) ||
-      make_tensor_map_3d(&mk, k, kBf16, D, Skv, BH, D, static_cast<uint64_t>(Skv) * D, 64, 128) ||
-      make_tensor_map_3d(&mv, v, kBf16, D, Skv, BH, D, static_cast<uint64_t>(Skv) * D, 64, 128) ||
-      make_tensor_map_3d(&mo, out, kBf16, D, Sq, BH, D, static_cast<uint64_t>(Sq) * D, 64, 128))
-    return ATTN_ERR_TENSOR_MAP;
+  const int r[4] = {
+      make_tensor_map_4d(&mq, q, kBf16, D, Sq, H, B, sq.l, sq.h, sq.b, 64, 128),
+      make_tensor_map_4d(&mk, k, kBf16, D, Skv, H, B, sk.l, sk.h, sk.b, 64, 128),
+      make_tensor_map_4d(&mv, v, kBf16, D, Skv, H, B, sv.l, sv.h, sv.b, 64, 128),
+      make_tensor_map_4d(&mo, out, kBf16, D, Sq, H, B, D, static_cast<uint64_t>(Sq) * D,
+                         static_cast<uint64_t>(H) * Sq * D, 64, 128)};
+  for (int e : r)
+    if (e == kNoTensorMap) return kNoTensorMap;
+  for (int e : r)
+    if (e != 0) return ATTN_ERR_TENSOR_MAP;
 
   auto kern = attn_fwd_kernel<kBf16, kD, kCausal>;
   // Opt in to the large dynamic shared-memory carve-out once per device.
@@ -678,7 +695,9 @@ static int launch_impl(const void* q, const void* k, const void* v, void* out, i
   AttnParams prm;
   prm.Lq = Sq;
   prm.Lk = Skv;
+  const int BH = B * H;
   prm.BH = BH;
+  prm.H = H;
   prm.num_qblocks = (Sq + 255) / 256;
   // K+V bytes of one head; about 48 MB of them (a third of L2) per group.
   const double kv_bytes = 2.0 * Skv * kD * 2;
@@ -707,9 +726,10 @@ static int check_device() {
 
 }  // namespace ra
 
-extern "C" int launch_attn_forward(const void* q, const void* k, const void* v, void* out, int B, int H, int Sq,
-                                   int Skv, int D, bool causal, float softmax_scale, AttnDType dtype,
-                                   cudaStream_t stream) {
+extern "C" int launch_attn_forward_strided(const void* q, const void* k, const void* v, void* out, int B, int H,
+                                           int Sq, int Skv, int D, bool causal, float softmax_scale, AttnDType dtype,
+                                           const long long* q_strides, const long long* k_strides,
+                                           const long long* v_strides, cudaStream_t stream) {
   using namespace ra;
   if (B < 0 || H < 0 || Sq < 0 || Skv < 0 || D <= 0) return ATTN_ERR_INVALID_ARGUMENT;
   if (dtype != ATTN_F16 && dtype != ATTN_BF16 && dtype != ATTN_F32) return ATTN_ERR_UNSUPPORTED;
@@ -718,6 +738,18 @@ extern "C" int launch_attn_forward(const void* q, const void* k, const void* v, 
   if (BH == 0 || Sq == 0) return ATTN_OK;  // empty output, nothing to do
   if (BH > 0x7fffffffLL) return ATTN_ERR_INVALID_ARGUMENT;
   if (!q || !out || (Skv > 0 && (!k || !v))) return ATTN_ERR_INVALID_ARGUMENT;
+  // Strides over (batch, head, row) in elements; null means contiguous.
+  auto strides_of = [&](const long long* st, int L, Strides* o) {
+    if (!st) {
+      *o = Strides{static_cast<long long>(H) * L * D, static_cast<long long>(L) * D, D};
+      return true;
+    }
+    *o = Strides{st[0], st[1], st[2]};
+    return o->b >= 0 && o->h >= 0 && o->l >= 0;
+  };
+  Strides sq, sk, sv;
+  if (!strides_of(q_strides, Sq, &sq) || !strides_of(k_strides, Skv, &sk) || !strides_of(v_strides, Skv, &sv))
+    return ATTN_ERR_INVALID_ARGUMENT;
   const size_t elem = dtype == ATTN_F32 ? 4 : 2;
   auto aligned = [](const void* ptr, size_t a) { return (reinterpret_cast<uintptr_t>(ptr) & (a - 1)) == 0; };
   if (!aligned(q, elem) || !aligned(out, elem) || (Skv > 0 && (!aligned(k, elem) || !aligned(v, elem))))
@@ -732,18 +764,23 @@ extern "C" int launch_attn_forward(const void* q, const void* k, const void* v, 
   }
   float scale = softmax_scale;
   if (!(scale > 0.f) || !isfinite(scale)) scale = 1.0f / sqrtf(static_cast<float>(D));
-  const int bh = static_cast<int>(BH);
-  // The tensor-core kernel takes fp16/bf16 with D in {64, 128} and TMA-ready
-  // (16-byte aligned) buffers; every other call runs the general kernel.
-  const bool tensor_path = dtype != ATTN_F32 && (D == 64 || D == 128) && aligned(q, 16) && aligned(out, 16) &&
-                           aligned(k, 16) && aligned(v, 16);
-  if (!tensor_path)
-    return launch_attn_general(q, k, v, out, bh, Sq, Skv, D, causal, scale, static_cast<int>(dtype), stream) == 0
+  const GeneralStrides gs{{sq.b, sq.h, sq.l}, {sk.b, sk.h, sk.l}, {sv.b, sv.h, sv.l}};
+  auto general = [&] {
+    return launch_attn_general(q, k, v, out, B, H, Sq, Skv, D, causal, scale, static_cast<int>(dtype), gs, stream) ==
+                   0
                ? ATTN_OK
                : ATTN_ERR_LAUNCH;
+  };
+  // The tensor-core kernel takes fp16/bf16 with D in {64, 128} and buffers
+  // TMA can describe (16-byte aligned base and strides); every other call
+  // runs the general kernel.
+  if (dtype == ATTN_F32 || (D != 64 && D != 128) || !aligned(out, 16)) return general();
   const bool bf16 = dtype == ATTN_BF16;
-#define RA_DISPATCH(BF, DD, CA) \
-  if (bf16 == BF && D == DD && causal == CA) return launch_impl<BF, DD, CA>(q, k, v, out, bh, Sq, Skv, scale, stream);
+  int st = ATTN_ERR_UNSUPPORTED;
+#define RA_DISPATCH(BF, DD, CA)                                                           \
+  if (bf16 == BF && D == DD && causal == CA)                                              \
+    st = launch_impl<BF, DD, CA>(q, k, v, out, B, H, Sq, Skv, sq, sk, sv, scale, stream); \
+  else
   RA_DISPATCH(false, 128, false)
   RA_DISPATCH(false, 128, true)
   RA_DISPATCH(false, 64, false)
@@ -751,9 +788,16 @@ extern "C" int launch_attn_forward(const void* q, const void* k, const void* v, 
   RA_DISPATCH(true, 128, false)
   RA_DISPATCH(true, 128, true)
   RA_DISPATCH(true, 64, false)
-  RA_DISPATCH(true, 64, true)
+  RA_DISPATCH(true, 64, true) {}
 #undef RA_DISPATCH
-  return ATTN_ERR_UNSUPPORTED;
+  return st == kNoTensorMap ? general() : st;
+}
+
+extern "C" int launch_attn_forward(const void* q, const void* k, const void* v, void* out, int B, int H, int Sq,
+                                   int Skv, int D, bool causal, float softmax_scale, AttnDType dtype,
+                                   cudaStream_t stream) {
+  return launch_attn_forward_strided(q, k, v, out, B, H, Sq, Skv, D, causal, softmax_scale, dtype, nullptr, nullptr,
+                                     nullptr, stream);
 }
 
 extern "C" int attn_get_status(cudaStream_t stream, int* status) {

@@ -1,7 +1,8 @@
 // PyTorch binding of the sm_100a attention launcher, module
 // `rocm_attn_ext`.  Mirrors the reference binding src/attn_torch.cpp:9-62 of
 // JoursBleu/rocm_attn (same checks and messages, same argument meaning), with
-// these changes: an optional softmax scale, the output from torch::empty (the
+// these changes: an optional softmax scale, inputs read through their strides
+// instead of copied to contiguous tensors, the output from torch::empty (the
 // kernel writes every element), the *current* stream of q's device, and a
 // launcher status mapped to a Python RuntimeError.
 #include <torch/extension.h>
@@ -43,9 +44,13 @@ static torch::Tensor attn_forward(torch::Tensor q, torch::Tensor k, torch::Tenso
   TORCH_CHECK(q.device() == k.device() && q.device() == v.device(), "q, k, v must be on the same device");
 
   const c10::cuda::CUDAGuard guard(q.device());
-  auto q_c = q.contiguous();
-  auto k_c = k.contiguous();
-  auto v_c = v.contiguous();
+  // Inputs whose head dim is contiguous are read in place through their
+  // strides (no copy, unlike the reference's .contiguous() calls); others are
+  // made contiguous first.
+  auto unit_inner = [](const torch::Tensor& t) { return t.dim() == 4 && (t.size(3) <= 1 || t.stride(3) == 1); };
+  auto q_c = unit_inner(q) ? q : q.contiguous();
+  auto k_c = unit_inner(k) ? k : k.contiguous();
+  auto v_c = unit_inner(v) ? v : v.contiguous();
 
   const int64_t B = q_c.size(0), H = q_c.size(1), Sq = q_c.size(2), D = q_c.size(3);
   const int64_t Skv = k_c.size(2);
@@ -56,17 +61,28 @@ static torch::Tensor attn_forward(torch::Tensor q, torch::Tensor k, torch::Tenso
   TORCH_CHECK(B <= INT32_MAX && H <= INT32_MAX && Sq <= INT32_MAX && Skv <= INT32_MAX,
               "sizes must fit in 32-bit integers");
 
-  auto out = torch::empty_like(q_c);
+  auto out = torch::empty({B, H, Sq, D}, q_c.options());
 
   AttnDType dtype = ATTN_F32;
   if (q.scalar_type() == torch::kFloat16) dtype = ATTN_F16;
   else if (q.scalar_type() == torch::kBFloat16) dtype = ATTN_BF16;
 
   cudaStream_t stream = at::cuda::getCurrentCUDAStream(q.device().index()).stream();
-  const int st = launch_attn_forward(q_c.data_ptr(), k_c.data_ptr(), v_c.data_ptr(), out.data_ptr(),
-                                     static_cast<int>(B), static_cast<int>(H), static_cast<int>(Sq),
-                                     static_cast<int>(Skv), static_cast<int>(D), causal,
-                                     static_cast<float>(scale), dtype, stream);
+  // Strides over (batch, head, row).  A dim of size 1 may carry any stride in
+  // torch; give it the contiguous one so TMA can take the tensor.
+  auto strides3 = [](const torch::Tensor& t, long long* s) {
+    s[2] = t.size(2) == 1 ? t.size(3) : t.stride(2);
+    s[1] = t.size(1) == 1 ? s[2] * t.size(2) : t.stride(1);
+    s[0] = t.size(0) == 1 ? s[1] * t.size(1) : t.stride(0);
+  };
+  long long qs[3], ks[3], vs[3];
+  strides3(q_c, qs);
+  strides3(k_c, ks);
+  strides3(v_c, vs);
+  const int st = launch_attn_forward_strided(q_c.data_ptr(), k_c.data_ptr(), v_c.data_ptr(), out.data_ptr(),
+                                             static_cast<int>(B), static_cast<int>(H), static_cast<int>(Sq),
+                                             static_cast<int>(Skv), static_cast<int>(D), causal,
+                                             static_cast<float>(scale), dtype, qs, ks, vs, stream);
   TORCH_CHECK(st == ATTN_OK, "launch_attn_forward: ", status_text(st), " (status ", st, ")");
   return out;
 }
