@@ -69,6 +69,9 @@ def parse_args(argv=None):
     ap.add_argument("--cpu-sample-seconds", type=float, default=12.0)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--graph", action="store_true",
+                    help="capture one step (all shapes of the workload) in a CUDA graph and time its replays: "
+                         "removes the per-launch host overhead of small-shape workloads")
     return ap.parse_args(argv)
 
 
@@ -270,6 +273,14 @@ def run_ours(args, rank, world, local_rank):
         step()
     torch.cuda.synchronize(dev)
     assert rocm_attn_op.check_status(local_rank) == 0, "kernel watchdog fired during warm-up"
+    run = step
+    if args.graph:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        graph.replay()
+        torch.cuda.synchronize(dev)
+        run = graph.replay
 
     # ---- timed region (device time, per step events, L2 flushed between steps)
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
@@ -281,7 +292,7 @@ def run_ours(args, rank, world, local_rank):
         for i in range(args.steps):
             flush.fill_(float(i))
             starts[i].record(stream)
-            step()
+            run()
             ends[i].record(stream)
         torch.cuda.synchronize(dev)
         if dist:
@@ -360,6 +371,7 @@ def run_ours(args, rank, world, local_rank):
         "config": {"workload": w.name, "shapes": [s.__dict__ for s in w.shapes], "causal": w.causal,
                    "sharding": "contiguous (batch*head) slices per rank, no collective in the timed region",
                    "l2": "256 MiB buffer rewritten between timed steps (outside the events)",
+                   "cuda_graph": bool(args.graph),
                    "frac_of_spec_dense_fp16": round(tflops / world / SPEC_DENSE_FP16_TFLOPS, 4)},
         "e2e": e2e,
         "gpu_launches": args.steps * sum(1 for _, r in shards if len(r) > 0),

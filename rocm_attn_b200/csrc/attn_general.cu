@@ -21,6 +21,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <string.h>
 
 #include "attn_general.h"
 
@@ -157,7 +158,233 @@ int launch_dims(const void* q, const void* k, const void* v, void* out, int BH, 
   return launch_typed<T, 256>(q, k, v, out, BH, H, Sq, Skv, D, causal, scale_log2, st, stream);
 }
 
+// ---------------------------------------------------------------------------
+// Short sequences (Sq <= 32, Skv <= 64): one warp per (batch, head) slice,
+// kSmallWarps warps per CTA walking the slices with a grid stride.  A warp
+// converts its slice's K and V to fp32 in its own shared-memory region; lane l
+// takes query row l / kLpr and the contiguous dims [kPer * (l % kLpr),
+// kPer * (l % kLpr + 1)), kLpr = 32 / (rows rounded up to a power of two).
+// With at most 64 keys a row keeps all its scores in registers: one max, one
+// exponential per key and one pass over V, with no running rescale.
+// This replaces a 256-row tensor-core tile per slice, which for the
+// reference's 16-row inference shapes would be 94% padding.
+// ---------------------------------------------------------------------------
+constexpr int kSmallWarps = 4;
+
+// 8 consecutive elements of a 16-byte aligned fp16/bf16/fp32 row as fp32.
+__device__ __forceinline__ void load_f32x8(const void* src, int dtype, float* dst) {
+  if (dtype == 2) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(src));
+    const float4 b = __ldg(reinterpret_cast<const float4*>(src) + 1);
+    dst[0] = a.x; dst[1] = a.y; dst[2] = a.z; dst[3] = a.w;
+    dst[4] = b.x; dst[5] = b.y; dst[6] = b.z; dst[7] = b.w;
+    return;
+  }
+  const uint4 raw = __ldg(reinterpret_cast<const uint4*>(src));
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 f;
+    if (dtype == 0) {
+      __half2 h;
+      memcpy(&h, &w[i], 4);
+      f = __half22float2(h);
+    } else {
+      __nv_bfloat162 h;
+      memcpy(&h, &w[i], 4);
+      f = __bfloat1622float2(h);
+    }
+    dst[2 * i] = f.x;
+    dst[2 * i + 1] = f.y;
+  }
+}
+
+// Lanes per query row of the short-sequence kernel at head dim D (each lane
+// holds 32 dims, 16 at D = 16): the warp covers 32 / lanes rows.
+__host__ __device__ constexpr int small_lanes_per_row(int D) { return D <= 32 ? 1 : D / 32; }
+
+// kD: the head dim (16, 32, 64 or 128); kKeys: the key capacity (16 or 64).
+// dtype and causal are the same for the whole launch.
+template <int kD, int kKeys>
+__global__ void __launch_bounds__(kSmallWarps * 32) attn_small_kernel(const void* __restrict__ q,
+                                                                      const void* __restrict__ k,
+                                                                      const void* __restrict__ v,
+                                                                      void* __restrict__ o, int dtype, bool causal,
+                                                                      int BH, int H, int Sq, int Skv,
+                                                                      float scale_log2, const GeneralStrides st) {
+  constexpr int kLpr = small_lanes_per_row(kD);
+  constexpr int kPer = kD / kLpr;
+  static_assert(kPer % 8 == 0, "lane runs are whole chunks of 8 elements");
+  extern __shared__ __align__(16) unsigned char small_smem[];
+  const int esize = dtype == 2 ? 4 : 2;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  float* sK = reinterpret_cast<float*>(small_smem) + static_cast<size_t>(warp) * 2 * kKeys * kD;
+  float* sV = sK + kKeys * kD;
+  const int row = lane / kLpr, d0 = (lane % kLpr) * kPer;
+  const bool live = row < Sq;
+  const char* qb = static_cast<const char*>(q);
+  const char* kb = static_cast<const char*>(k);
+  const char* vb = static_cast<const char*>(v);
+
+  for (int bh = blockIdx.x * kSmallWarps + warp; bh < BH; bh += gridDim.x * kSmallWarps) {
+    const long long b = bh / H, h = bh - b * H;
+    const long long k0 = b * st.k[0] + h * st.k[1], v0 = b * st.v[0] + h * st.v[1];
+    __syncwarp();  // the previous slice's keys are no longer read
+    for (int e = lane; e < Skv * (kD / 8); e += 32) {
+      const int key = e / (kD / 8), c = (e - key * (kD / 8)) * 8;
+      float a[8], w[8];
+      load_f32x8(kb + (k0 + key * st.k[2] + c) * esize, dtype, a);
+      load_f32x8(vb + (v0 + key * st.v[2] + c) * esize, dtype, w);
+      float4* dk = reinterpret_cast<float4*>(sK + key * kD + c);
+      float4* dv = reinterpret_cast<float4*>(sV + key * kD + c);
+      dk[0] = make_float4(a[0], a[1], a[2], a[3]);
+      dk[1] = make_float4(a[4], a[5], a[6], a[7]);
+      dv[0] = make_float4(w[0], w[1], w[2], w[3]);
+      dv[1] = make_float4(w[4], w[5], w[6], w[7]);
+    }
+    __syncwarp();
+
+    float qr[kPer];
+    {
+      const long long q0 = b * st.q[0] + h * st.q[1] + static_cast<long long>(live ? row : 0) * st.q[2] + d0;
+#pragma unroll
+      for (int i = 0; i < kPer; i += 8) load_f32x8(qb + (q0 + i) * esize, dtype, qr + i);
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) qr[i] *= scale_log2;
+    }
+    const int key_end = causal ? min(Skv, row + 1) : Skv;
+    float s[kKeys];
+    float m = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < kKeys; ++j) {
+      s[j] = -INFINITY;
+      if (j < Skv) {  // uniform across the warp
+        const float4* kr = reinterpret_cast<const float4*>(sK + j * kD + d0);
+        float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+        for (int i = 0; i < kPer / 4; ++i) {
+          const float4 x = kr[i];
+          a0 = fmaf(qr[4 * i], x.x, a0);
+          a1 = fmaf(qr[4 * i + 1], x.y, a1);
+          a0 = fmaf(qr[4 * i + 2], x.z, a0);
+          a1 = fmaf(qr[4 * i + 3], x.w, a1);
+        }
+        float dot = a0 + a1;
+#pragma unroll
+        for (int off = 1; off < kLpr; off <<= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
+        if (j < key_end) s[j] = dot;
+        m = fmaxf(m, s[j]);
+      }
+    }
+    float l = 0.f;
+#pragma unroll
+    for (int j = 0; j < kKeys; ++j) {
+      s[j] = j < Skv ? exp2f(s[j] - m) : 0.f;  // a masked key gives 0
+      l += s[j];
+    }
+    float acc[kPer];
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) acc[i] = 0.f;
+#pragma unroll
+    for (int j = 0; j < kKeys; ++j)
+      if (j < Skv) {
+        const float4* vr = reinterpret_cast<const float4*>(sV + j * kD + d0);
+#pragma unroll
+        for (int i = 0; i < kPer / 4; ++i) {
+          const float4 x = vr[i];
+          acc[4 * i] = fmaf(s[j], x.x, acc[4 * i]);
+          acc[4 * i + 1] = fmaf(s[j], x.y, acc[4 * i + 1]);
+          acc[4 * i + 2] = fmaf(s[j], x.z, acc[4 * i + 2]);
+          acc[4 * i + 3] = fmaf(s[j], x.w, acc[4 * i + 3]);
+        }
+      }
+    if (live) {
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const size_t o0 = (static_cast<size_t>(bh) * Sq + row) * kD + d0;
+      if (dtype == 2) {
+        float4* orow = reinterpret_cast<float4*>(static_cast<float*>(o) + o0);
+#pragma unroll
+        for (int i = 0; i < kPer / 4; ++i)
+          orow[i] = make_float4(acc[4 * i] * inv, acc[4 * i + 1] * inv, acc[4 * i + 2] * inv, acc[4 * i + 3] * inv);
+      } else {
+        uint4* orow = reinterpret_cast<uint4*>(static_cast<char*>(o) + o0 * 2);
+#pragma unroll
+        for (int i = 0; i < kPer / 8; ++i) {
+          uint32_t w[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const float lo = acc[8 * i + 2 * u] * inv, hi = acc[8 * i + 2 * u + 1] * inv;
+            if (dtype == 0) {
+              const __half2 hh = __floats2half2_rn(lo, hi);
+              memcpy(&w[u], &hh, 4);
+            } else {
+              const __nv_bfloat162 hh = __floats2bfloat162_rn(lo, hi);
+              memcpy(&w[u], &hh, 4);
+            }
+          }
+          orow[i] = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
+    }
+  }
+}
+
+template <int kD, int kKeys>
+int launch_small_typed(const void* q, const void* k, const void* v, void* out, int dtype, bool causal, int BH, int H,
+                       int Sq, int Skv, float scale_log2, const GeneralStrides& st, cudaStream_t stream) {
+  const int smem = kSmallWarps * 2 * kKeys * kD * static_cast<int>(sizeof(float));
+  auto kern = attn_small_kernel<kD, kKeys>;
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return -1;
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return -1;
+  const long long need = (static_cast<long long>(BH) + kSmallWarps - 1) / kSmallWarps;
+  const unsigned grid = static_cast<unsigned>(need < 32LL * sms ? need : 32LL * sms);
+  kern<<<grid, kSmallWarps * 32, smem, stream>>>(q, k, v, out, dtype, causal, BH, H, Sq, Skv, scale_log2, st);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+template <int kD>
+int launch_small_keys(const void* q, const void* k, const void* v, void* out, int dtype, bool causal, int BH, int H,
+                      int Sq, int Skv, float scale_log2, const GeneralStrides& st, cudaStream_t stream) {
+  if (Skv <= 16)
+    return launch_small_typed<kD, 16>(q, k, v, out, dtype, causal, BH, H, Sq, Skv, scale_log2, st, stream);
+  return launch_small_typed<kD, 64>(q, k, v, out, dtype, causal, BH, H, Sq, Skv, scale_log2, st, stream);
+}
+
 }  // namespace
+
+bool small_kernel_takes(int Sq, int Skv, int D, int dtype) {
+  (void)dtype;
+  if (D != 16 && D != 32 && D != 64 && D != 128) return false;
+  return Sq >= 1 && Sq <= 32 / small_lanes_per_row(D) && Skv >= 1 && Skv <= kSmallMaxKeys;
+}
+
+int launch_attn_small(const void* q, const void* k, const void* v, void* out, int B, int H, int Sq, int Skv, int D,
+                      bool causal, float scale, int dtype, const GeneralStrides& st, cudaStream_t stream) {
+  const long long BH = static_cast<long long>(B) * H;
+  if (B <= 0 || H <= 0 || BH > 0x7fffffffLL || dtype < 0 || dtype > 2 || !small_kernel_takes(Sq, Skv, D, dtype))
+    return -1;
+  // 16-byte chunks: the bases and the row/head/batch strides must keep every
+  // row 16-byte aligned.
+  const long long esize = dtype == 2 ? 4 : 2;
+  auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  for (const long long* s3 : {st.q, st.k, st.v})
+    for (int i = 0; i < 3; ++i)
+      if ((s3[i] * esize) % 16 != 0) return -2;
+  if (!a16(q) || !a16(k) || !a16(v) || !a16(out)) return -2;
+  const int bh = static_cast<int>(BH);
+  const float sl = scale * 1.4426950408889634f;
+  switch (D) {
+    case 16: return launch_small_keys<16>(q, k, v, out, dtype, causal, bh, H, Sq, Skv, sl, st, stream);
+    case 32: return launch_small_keys<32>(q, k, v, out, dtype, causal, bh, H, Sq, Skv, sl, st, stream);
+    case 64: return launch_small_keys<64>(q, k, v, out, dtype, causal, bh, H, Sq, Skv, sl, st, stream);
+    default: return launch_small_keys<128>(q, k, v, out, dtype, causal, bh, H, Sq, Skv, sl, st, stream);
+  }
+}
 
 int launch_attn_general(const void* q, const void* k, const void* v, void* out, int B, int H, int Sq, int Skv,
                         int D, bool causal, float scale, int dtype, const GeneralStrides& st, cudaStream_t stream) {

@@ -24,4 +24,18 @@ int launch_attn_general(const void* q, const void* k, const void* v, void* out, 
                         int D, bool causal, float scale, int dtype, const GeneralStrides& strides,
                         cudaStream_t stream);
 
+// Bounds of the short-sequence kernel (one warp per (batch, head) slice with
+// the slice's K and V in shared memory as fp32): D in {16, 32, 64, 128}, Skv
+// <= kSmallMaxKeys, Sq <= 32 rows at D <= 32, 16 at D = 64, 8 at D = 128.
+constexpr int kSmallMaxKeys = 64;
+
+// True when launch_attn_small takes a problem of these sizes.
+bool small_kernel_takes(int Sq, int Skv, int D, int dtype);
+
+// Same contract as launch_attn_general for problems small_kernel_takes, and
+// buffers whose bases and strides keep each row 16-byte aligned; returns -2
+// (nothing launched) when they do not.
+int launch_attn_small(const void* q, const void* k, const void* v, void* out, int B, int H, int Sq, int Skv, int D,
+                      bool causal, float scale, int dtype, const GeneralStrides& strides, cudaStream_t stream);
+
 }  // namespace ra

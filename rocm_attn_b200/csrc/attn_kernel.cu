@@ -771,6 +771,12 @@ extern "C" int launch_attn_forward_strided(const void* q, const void* k, const v
                ? ATTN_OK
                : ATTN_ERR_LAUNCH;
   };
+  // Short sequences (a few dozen rows per head): one warp per (batch, head)
+  // slice instead of a mostly empty 256-row tile.
+  if (small_kernel_takes(Sq, Skv, D, static_cast<int>(dtype)))
+    return launch_attn_small(q, k, v, out, B, H, Sq, Skv, D, causal, scale, static_cast<int>(dtype), gs, stream) == 0
+               ? ATTN_OK
+               : ATTN_ERR_LAUNCH;
   // The tensor-core kernel takes fp16/bf16 with D in {64, 128} and buffers
   // TMA can describe (16-byte aligned base and strides); every other call
   // runs the general kernel.

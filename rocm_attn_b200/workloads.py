@@ -70,6 +70,16 @@ WORKLOADS = {
                     Shape(16, 8, 128, 128, 128), Shape(1, 32, 8192, 8192, 128)), "fp16", False),
 }
 
+# The reference's inference shape set for its production caller, UnifoLM-WMA
+# (benchmark/attn_shapes_unifolm_infer.txt:1-17, run by
+# benchmark/run_preset_benchmarks.sh:7-22 as fp16, non-causal): huge B*H with
+# short sequences, and cross attention with 93 or 351 keys.
+UNIFOLM_SHAPES = (
+    "2560,8,16,64;16,5,2560,64;2560,5,16,64;16,10,640,64;640,10,16,64;16,20,160,64;160,20,16,64;"
+    "16,20,40,64;40,20,16,64;16,5,2560,93,64;16,10,640,93,64;16,20,160,93,64;16,20,40,93,64;"
+    "16,5,2560,351,64;16,10,640,351,64;16,20,160,351,64;16,20,40,351,64"
+)
+
 _TENSOR_ID = {"q": 0, "k": 1, "v": 2}
 
 
@@ -137,6 +147,10 @@ def parse_shapes(spec: str) -> list[Shape]:
     if not shapes:
         raise ValueError("--shapes is empty")
     return shapes
+
+
+WORKLOADS["unifolm"] = Workload("unifolm-infer-17-shapes-noncausal-fp16", tuple(parse_shapes(UNIFOLM_SHAPES)),
+                                "fp16", False)
 
 
 def iter_flops(shapes: Iterable[Shape], causal: bool) -> float:
