@@ -65,5 +65,7 @@ def check_status(device: int = 0) -> int:
     return int(rocm_attn_ext.check_status(int(device)))
 
 
-__all__ = ["attn_forward", "check_status", "rocm_attn_ext", "KERNEL_LIB_PATH",
+from .pipeline import attn_forward_pinned  # noqa: E402  (host-resident inputs, transfers overlapped)
+
+__all__ = ["attn_forward", "attn_forward_pinned", "check_status", "rocm_attn_ext", "KERNEL_LIB_PATH",
            "SUPPORTED_HEAD_DIMS", "SUPPORTED_DTYPES", "MAX_HEAD_DIM"]

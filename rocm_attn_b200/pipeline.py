@@ -1,0 +1,101 @@
+"""Attention on host-resident tensors with the transfers overlapped.
+
+``attn_forward_pinned`` is the public entry for callers whose q/k/v live in
+pinned host memory (the end-to-end path of the benchmark).  It splits the
+flattened (batch, head) slices into chunks and keeps three CUDA streams busy:
+the host-to-device copy of chunk c+1, the attention of chunk c (the caller's
+current stream, through ``attn_forward``) and the device-to-host copy of
+chunk c-1 run at the same time, so a step costs about the larger of the two
+PCIe directions instead of their sum plus the compute.  The reference has no
+counterpart: its callers copy whole tensors and call the op
+(benchmark/bench_attention.py:178-184).
+"""
+from __future__ import annotations
+
+import math
+import threading
+from typing import Optional
+
+import torch
+
+_lock = threading.Lock()
+_state: dict = {}
+
+
+def _device_state(device: torch.device, key: tuple, q_shape, k_shape, dtype):
+    """Device buffers and events for one (device, shape, dtype, chunking),
+    reused across calls so a steady caller allocates nothing."""
+    with _lock:
+        st = _state.get(key)
+        if st is None:
+            st = {
+                "q": torch.empty(q_shape, dtype=dtype, device=device),
+                "k": torch.empty(k_shape, dtype=dtype, device=device),
+                "v": torch.empty(k_shape, dtype=dtype, device=device),
+                "s_in": torch.cuda.Stream(device=device),
+                "s_out": torch.cuda.Stream(device=device),
+                "done": {},  # chunk -> event recorded after its attention was queued
+            }
+            _state[key] = st
+        return st
+
+
+def attn_forward_pinned(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = False,
+                        scale: Optional[float] = None, out: Optional[torch.Tensor] = None,
+                        chunk_slices: Optional[int] = None, device: Optional[torch.device] = None) -> torch.Tensor:
+    """Attention forward for contiguous pinned host tensors q [B, H, Lq, D],
+    k/v [B, H, Lk, D].  Returns O [B, H, Lq, D] in pinned host memory (``out``
+    if given).  Asynchronous like the op itself: the result is ready once the
+    caller's current stream on ``device`` is synchronised.  ``chunk_slices``
+    (batch, head) slices go per chunk (default: about eight chunks)."""
+    from . import attn_forward
+
+    if device is None:
+        device = torch.device("cuda", torch.cuda.current_device())
+    for t in (q, k, v):
+        if t.device.type != "cpu" or not t.is_contiguous():
+            raise ValueError("attn_forward_pinned takes contiguous host tensors")
+    B, H, Lq, D = q.shape
+    Lk = k.shape[2]
+    BH = B * H
+    if out is None:
+        out = torch.empty((B, H, Lq, D), dtype=q.dtype, pin_memory=True)
+    if BH == 0 or Lq == 0:
+        return out
+    n = chunk_slices or max(1, math.ceil(BH / 8))
+    chunks = [(c0, min(BH, c0 + n)) for c0 in range(0, BH, n)]
+    key = (device, tuple(q.shape), tuple(k.shape), q.dtype, n)
+    st = _device_state(device, key, (BH, Lq, D), (BH, Lk, D), q.dtype)
+    hq, hk, hv, ho = (t.view(BH, -1, D) for t in (q, k, v, out))
+    compute = torch.cuda.current_stream(device)
+    s_in, s_out = st["s_in"], st["s_out"]
+    start = torch.cuda.Event()
+    start.record(compute)
+    for i, (c0, c1) in enumerate(chunks):
+        # inputs of chunk i: after earlier work on the caller's stream and
+        # after the previous call's attention read these device buffers
+        s_in.wait_event(start)
+        prev = st["done"].get(i)
+        if prev is not None:
+            s_in.wait_event(prev)
+        with torch.cuda.stream(s_in):
+            st["q"][c0:c1].copy_(hq[c0:c1], non_blocking=True)
+            st["k"][c0:c1].copy_(hk[c0:c1], non_blocking=True)
+            st["v"][c0:c1].copy_(hv[c0:c1], non_blocking=True)
+        ready = torch.cuda.Event()
+        ready.record(s_in)
+        compute.wait_event(ready)
+        o = attn_forward(st["q"][c0:c1].unsqueeze(0), st["k"][c0:c1].unsqueeze(0), st["v"][c0:c1].unsqueeze(0),
+                         causal=causal, scale=scale)
+        done = torch.cuda.Event()
+        done.record(compute)
+        st["done"][i] = done
+        s_out.wait_event(done)
+        with torch.cuda.stream(s_out):
+            ho[c0:c1].copy_(o[0], non_blocking=True)
+        o.record_stream(s_out)
+    compute.wait_stream(s_out)
+    return out
+
+
+__all__ = ["attn_forward_pinned"]
