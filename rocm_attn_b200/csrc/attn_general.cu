@@ -355,6 +355,224 @@ int launch_small_keys(const void* q, const void* k, const void* v, void* out, in
   return launch_small_typed<kD, 64>(q, k, v, out, dtype, causal, BH, H, Sq, Skv, scale_log2, st, stream);
 }
 
+// ---------------------------------------------------------------------------
+// Short sequences on the warp-level tensor-core path (fp16/bf16, Sq <= 16,
+// Skv <= 64, D in {16, 32, 64, 128}): one warp per (batch, head) slice does
+// S = Q K^T and O = P V with mma.sync m16n8k16 (fp32 accumulate).  Q, K and V
+// are staged in the warp's shared memory in rows padded by 16 bytes (so the
+// eight row addresses of an ldmatrix hit distinct banks) and read as
+// fragments with ldmatrix (V transposed).  The accumulator fragments of S are
+// the A fragments of P V after packing to 16-bit pairs, so P never leaves
+// registers.  Row max and sum reduce over the four lanes of a row quad.
+// ---------------------------------------------------------------------------
+constexpr int kMmaWarps = 4;
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+template <bool kBf16>
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  if constexpr (kBf16) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+                 "{%8, %9}, {%0, %1, %2, %3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  } else {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+                 "{%8, %9}, {%0, %1, %2, %3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+}
+template <bool kBf16>
+__device__ __forceinline__ uint32_t pack16x2(float lo, float hi) {
+  uint32_t w;
+  if constexpr (kBf16) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    memcpy(&w, &h, 4);
+  } else {
+    const __half2 h = __floats2half2_rn(lo, hi);
+    memcpy(&w, &h, 4);
+  }
+  return w;
+}
+
+// kNK: 16-key groups (Skv <= 16 kNK).
+template <bool kBf16, int kD, int kNK>
+__global__ void __launch_bounds__(kMmaWarps * 32) attn_small_mma_kernel(const uint16_t* __restrict__ q,
+                                                                        const uint16_t* __restrict__ k,
+                                                                        const uint16_t* __restrict__ v,
+                                                                        uint16_t* __restrict__ o, bool causal,
+                                                                        int BH, int H, int Sq, int Skv,
+                                                                        float scale_log2, const GeneralStrides st) {
+  constexpr int kRow = kD + 8;        // padded row of a staged matrix, in 16-bit elements
+  constexpr int kKeys = 16 * kNK;
+  constexpr int kChunks = kD / 8;     // 16-byte chunks per row
+  extern __shared__ __align__(16) unsigned char mma_smem[];
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  uint16_t* sQ = reinterpret_cast<uint16_t*>(mma_smem) + static_cast<size_t>(warp) * (16 + 2 * kKeys) * kRow;
+  uint16_t* sK = sQ + 16 * kRow;
+  uint16_t* sV = sK + kKeys * kRow;
+  const int g = lane >> 2, t4 = lane & 3;  // row within an 8-row group, lane within the row quad
+  const int mi = lane >> 3, ri = lane & 7; // ldmatrix: matrix and row this lane addresses
+
+  for (int bh = blockIdx.x * kMmaWarps + warp; bh < BH; bh += gridDim.x * kMmaWarps) {
+    const long long b = bh / H, h = bh - b * H;
+    const uint16_t* qp = q + b * st.q[0] + h * st.q[1];
+    const uint16_t* kp = k + b * st.k[0] + h * st.k[1];
+    const uint16_t* vp = v + b * st.v[0] + h * st.v[1];
+    __syncwarp();  // the previous slice's staging is no longer read
+    // Stage Q (16 rows) and K, V (kKeys rows) in 16-byte chunks, zero past Sq / Skv.
+    for (int e = lane; e < (16 + 2 * kKeys) * kChunks; e += 32) {
+      const int r = e / kChunks, c = (e - r * kChunks) * 8;
+      uint4 val = make_uint4(0, 0, 0, 0);
+      uint16_t* dst;
+      if (r < 16) {
+        if (r < Sq) val = __ldg(reinterpret_cast<const uint4*>(qp + r * st.q[2] + c));
+        dst = sQ + r * kRow + c;
+      } else if (r < 16 + kKeys) {
+        const int key = r - 16;
+        if (key < Skv) val = __ldg(reinterpret_cast<const uint4*>(kp + key * st.k[2] + c));
+        dst = sK + key * kRow + c;
+      } else {
+        const int key = r - 16 - kKeys;
+        if (key < Skv) val = __ldg(reinterpret_cast<const uint4*>(vp + key * st.v[2] + c));
+        dst = sV + key * kRow + c;
+      }
+      *reinterpret_cast<uint4*>(dst) = val;
+    }
+    __syncwarp();
+
+    // S = Q K^T: 2 * kNK n8 tiles of keys, kD / 16 k-steps over the head dim.
+    float sf[2 * kNK][4];
+#pragma unroll
+    for (int n = 0; n < 2 * kNK; ++n) sf[n][0] = sf[n][1] = sf[n][2] = sf[n][3] = 0.f;
+    const uint32_t q_base = static_cast<uint32_t>(__cvta_generic_to_shared(sQ));
+    const uint32_t k_base = static_cast<uint32_t>(__cvta_generic_to_shared(sK));
+    const uint32_t v_base = static_cast<uint32_t>(__cvta_generic_to_shared(sV));
+#pragma unroll
+    for (int ks = 0; ks < kD / 16; ++ks) {
+      uint32_t a[4];
+      ldsm_x4(q_base + 2 * (((mi & 1) * 8 + ri) * kRow + ks * 16 + (mi >> 1) * 8), a);
+#pragma unroll
+      for (int nk = 0; nk < kNK; ++nk) {
+        uint32_t bk[4];
+        ldsm_x4(k_base + 2 * ((nk * 16 + (mi >> 1) * 8 + ri) * kRow + ks * 16 + (mi & 1) * 8), bk);
+        mma16816<kBf16>(sf[2 * nk], a, bk[0], bk[1]);
+        mma16816<kBf16>(sf[2 * nk + 1], a, bk[2], bk[3]);
+      }
+    }
+
+    // Softmax over each row (rows g and g + 8 of this lane; its keys are
+    // 8 n + 2 t4 and + 1 of every tile n).
+    float m0 = -INFINITY, m1 = -INFINITY;
+#pragma unroll
+    for (int n = 0; n < 2 * kNK; ++n) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int key = 8 * n + 2 * t4 + (e & 1);
+        const int row = g + (e >> 1) * 8;
+        const bool masked = key >= Skv || (causal && key > row);
+        sf[n][e] = masked ? -INFINITY : sf[n][e] * scale_log2;
+      }
+      m0 = fmaxf(m0, fmaxf(sf[n][0], sf[n][1]));
+      m1 = fmaxf(m1, fmaxf(sf[n][2], sf[n][3]));
+    }
+    m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, 1));
+    m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, 2));
+    m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, 1));
+    m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, 2));
+    float l0 = 0.f, l1 = 0.f;
+#pragma unroll
+    for (int n = 0; n < 2 * kNK; ++n) {
+      sf[n][0] = exp2f(sf[n][0] - m0);
+      sf[n][1] = exp2f(sf[n][1] - m0);
+      sf[n][2] = exp2f(sf[n][2] - m1);
+      sf[n][3] = exp2f(sf[n][3] - m1);
+      l0 += sf[n][0] + sf[n][1];
+      l1 += sf[n][2] + sf[n][3];
+    }
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+
+    // O = P V: P's accumulator fragments are A fragments after packing.
+    float of[kD / 8][4];
+#pragma unroll
+    for (int n = 0; n < kD / 8; ++n) of[n][0] = of[n][1] = of[n][2] = of[n][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < kNK; ++kk) {
+      const uint32_t a[4] = {pack16x2<kBf16>(sf[2 * kk][0], sf[2 * kk][1]),
+                             pack16x2<kBf16>(sf[2 * kk][2], sf[2 * kk][3]),
+                             pack16x2<kBf16>(sf[2 * kk + 1][0], sf[2 * kk + 1][1]),
+                             pack16x2<kBf16>(sf[2 * kk + 1][2], sf[2 * kk + 1][3])};
+#pragma unroll
+      for (int dt = 0; dt < kD / 8; dt += 2) {
+        uint32_t bv[4];
+        ldsm_x4_trans(v_base + 2 * ((kk * 16 + (mi & 1) * 8 + ri) * kRow + (dt + (mi >> 1)) * 8), bv);
+        mma16816<kBf16>(of[dt], a, bv[0], bv[1]);
+        mma16816<kBf16>(of[dt + 1], a, bv[2], bv[3]);
+      }
+    }
+    const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f, inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
+    uint16_t* ob = o + static_cast<size_t>(bh) * Sq * kD;
+#pragma unroll
+    for (int n = 0; n < kD / 8; ++n) {
+      const int col = 8 * n + 2 * t4;
+      if (g < Sq) *reinterpret_cast<uint32_t*>(ob + g * kD + col) = pack16x2<kBf16>(of[n][0] * inv0, of[n][1] * inv0);
+      if (g + 8 < Sq)
+        *reinterpret_cast<uint32_t*>(ob + (g + 8) * kD + col) = pack16x2<kBf16>(of[n][2] * inv1, of[n][3] * inv1);
+    }
+  }
+}
+
+template <bool kBf16, int kD, int kNK>
+int launch_small_mma_typed(const void* q, const void* k, const void* v, void* out, bool causal, int BH, int H, int Sq,
+                           int Skv, float scale_log2, const GeneralStrides& st, cudaStream_t stream) {
+  const int smem = kMmaWarps * (16 + 2 * 16 * kNK) * (kD + 8) * 2;
+  auto kern = attn_small_mma_kernel<kBf16, kD, kNK>;
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return -1;
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return -1;
+  const long long need = (static_cast<long long>(BH) + kMmaWarps - 1) / kMmaWarps;
+  const unsigned grid = static_cast<unsigned>(need < 32LL * sms ? need : 32LL * sms);
+  kern<<<grid, kMmaWarps * 32, smem, stream>>>(static_cast<const uint16_t*>(q), static_cast<const uint16_t*>(k),
+                                               static_cast<const uint16_t*>(v), static_cast<uint16_t*>(out), causal,
+                                               BH, H, Sq, Skv, scale_log2, st);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+template <bool kBf16, int kD>
+int launch_small_mma_keys(const void* q, const void* k, const void* v, void* out, bool causal, int BH, int H, int Sq,
+                          int Skv, float sl, const GeneralStrides& st, cudaStream_t stream) {
+  if (Skv <= 16) return launch_small_mma_typed<kBf16, kD, 1>(q, k, v, out, causal, BH, H, Sq, Skv, sl, st, stream);
+  if (Skv <= 32) return launch_small_mma_typed<kBf16, kD, 2>(q, k, v, out, causal, BH, H, Sq, Skv, sl, st, stream);
+  return launch_small_mma_typed<kBf16, kD, 4>(q, k, v, out, causal, BH, H, Sq, Skv, sl, st, stream);
+}
+
+template <bool kBf16>
+int launch_small_mma(const void* q, const void* k, const void* v, void* out, bool causal, int BH, int H, int Sq,
+                     int Skv, int D, float sl, const GeneralStrides& st, cudaStream_t stream) {
+  switch (D) {
+    case 16: return launch_small_mma_keys<kBf16, 16>(q, k, v, out, causal, BH, H, Sq, Skv, sl, st, stream);
+    case 32: return launch_small_mma_keys<kBf16, 32>(q, k, v, out, causal, BH, H, Sq, Skv, sl, st, stream);
+    case 64: return launch_small_mma_keys<kBf16, 64>(q, k, v, out, causal, BH, H, Sq, Skv, sl, st, stream);
+    default: return launch_small_mma_keys<kBf16, 128>(q, k, v, out, causal, BH, H, Sq, Skv, sl, st, stream);
+  }
+}
+
 }  // namespace
 
 bool small_kernel_takes(int Sq, int Skv, int D, int dtype) {
@@ -378,6 +596,11 @@ int launch_attn_small(const void* q, const void* k, const void* v, void* out, in
   if (!a16(q) || !a16(k) || !a16(v) || !a16(out)) return -2;
   const int bh = static_cast<int>(BH);
   const float sl = scale * 1.4426950408889634f;
+  // fp16/bf16 slices of up to 16 rows: warp-level tensor cores.
+  if (dtype != 2 && Sq <= 16) {
+    return dtype == 1 ? launch_small_mma<true>(q, k, v, out, causal, bh, H, Sq, Skv, D, sl, st, stream)
+                      : launch_small_mma<false>(q, k, v, out, causal, bh, H, Sq, Skv, D, sl, st, stream);
+  }
   switch (D) {
     case 16: return launch_small_keys<16>(q, k, v, out, dtype, causal, bh, H, Sq, Skv, sl, st, stream);
     case 32: return launch_small_keys<32>(q, k, v, out, dtype, causal, bh, H, Sq, Skv, sl, st, stream);
