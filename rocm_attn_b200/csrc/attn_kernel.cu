@@ -49,7 +49,7 @@ __device__ unsigned long long g_attn_trace[kTraceSlots];
 __device__ int g_attn_trace_cta = 0;
 #define RA_MARK(idx)                                                                      \
   do {                                                                                    \
-    if ((threadIdx.x & 31) == 0 && static_cast<int>(blockIdx.x) == g_attn_trace_cta &&    \
+    if ((threadIdx.x & 31) == 0 && ra_traced &&                                           \
         (idx) < kTraceSlots)                                                              \
       g_attn_trace[(idx)] = clock64();                                                    \
   } while (0)
@@ -165,6 +165,9 @@ __global__ void __launch_bounds__(320, 1)
 
   const int warp = __shfl_sync(0xffffffffu, static_cast<int>(threadIdx.x) / 32, 0);
   const int lane = threadIdx.x & 31;
+#ifdef RA_TRACE
+  const bool ra_traced = static_cast<int>(blockIdx.x) == g_attn_trace_cta;  // read once, not per mark
+#endif
 
   // Work unit (bh, qb).  Non-causal: every unit costs the same; the query
   // blocks of a head are adjacent so its K/V stay hot in L2.  Causal: unit
