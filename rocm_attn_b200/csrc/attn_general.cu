@@ -573,7 +573,239 @@ int launch_small_mma(const void* q, const void* k, const void* v, void* out, boo
   }
 }
 
+// ---------------------------------------------------------------------------
+// Mid-length sequences on warp-level tensor cores (fp16/bf16, D in {16, 32,
+// 64, 128}, any Skv; the dispatcher uses it for D = 16 / 32 and for short
+// D = 64 problems): FlashAttention-2-style.  A CTA of 4 warps takes 64
+// query rows of one (batch, head) slice, one m16 tile per warp; K and V stream
+// through shared memory in 64-key chunks, double-buffered with cp.async
+// (16-byte copies, zero-filled past Skv), rows padded by 16 bytes for
+// conflict-free ldmatrix.  Per chunk each warp computes S = Q K^T with
+// mma.sync m16n8k16 (fp32 accumulate), moves its running row max, rescales O
+// and the row sums, and adds P V with P taken straight from the S fragments.
+// ---------------------------------------------------------------------------
+constexpr int kMidWarps = 4;  // 64 query rows per CTA
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+template <bool kBf16, int kD>
+__global__ void __launch_bounds__(kMidWarps * 32) attn_mid_mma_kernel(const uint16_t* __restrict__ q,
+                                                                      const uint16_t* __restrict__ k,
+                                                                      const uint16_t* __restrict__ v,
+                                                                      uint16_t* __restrict__ o, bool causal, int H,
+                                                                      int Sq, int Skv, float scale_log2,
+                                                                      const GeneralStrides st) {
+  constexpr int kRow = kD + 8;
+  constexpr int kChunks = kD / 8;
+  constexpr int kThreads = kMidWarps * 32;
+  extern __shared__ __align__(16) unsigned char mid_smem[];
+  uint16_t* sQ = reinterpret_cast<uint16_t*>(mid_smem);  // [64][kRow]
+  uint16_t* sKV = sQ + 64 * kRow;                         // [2 buffers][K, V][64][kRow]
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t4 = lane & 3, mi = lane >> 3, ri = lane & 7;
+  const int mblocks = (Sq + 63) / 64;
+  const int bh = static_cast<int>(blockIdx.x) / mblocks;
+  const int row0 = (static_cast<int>(blockIdx.x) - bh * mblocks) * 64;
+  const long long b = bh / H, h = bh - b * H;
+  const uint16_t* qp = q + b * st.q[0] + h * st.q[1];
+  const uint16_t* kp = k + b * st.k[0] + h * st.k[1];
+  const uint16_t* vp = v + b * st.v[0] + h * st.v[1];
+  const int key_end = causal ? min(Skv, min(Sq, row0 + 64)) : Skv;  // keys this CTA's rows can see
+  const int nchunks = (key_end + 63) / 64;
+
+  auto load_chunk = [&](int c, int buf) {
+    uint16_t* dK = sKV + buf * 2 * 64 * kRow;
+    uint16_t* dV = dK + 64 * kRow;
+    for (int e = threadIdx.x; e < 64 * kChunks; e += kThreads) {
+      const int r = e / kChunks, col = (e - r * kChunks) * 8;
+      const int key = c * 64 + r;
+      const bool in = key < Skv;
+      const long long kr = in ? key : 0;
+      cp_async16(static_cast<uint32_t>(__cvta_generic_to_shared(dK + r * kRow + col)), kp + kr * st.k[2] + col, in);
+      cp_async16(static_cast<uint32_t>(__cvta_generic_to_shared(dV + r * kRow + col)), vp + kr * st.v[2] + col, in);
+    }
+  };
+  for (int e = threadIdx.x; e < 64 * kChunks; e += kThreads) {
+    const int r = e / kChunks, col = (e - r * kChunks) * 8;
+    const bool in = row0 + r < Sq;
+    const long long qr = in ? row0 + r : 0;
+    cp_async16(static_cast<uint32_t>(__cvta_generic_to_shared(sQ + r * kRow + col)), qp + qr * st.q[2] + col, in);
+  }
+  load_chunk(0, 0);
+  cp_async_commit();
+
+  const int rowA = row0 + warp * 16 + g, rowB = rowA + 8;  // this lane's two query rows
+  uint32_t qa[kD / 16][4];
+  float of[kD / 8][4];
+#pragma unroll
+  for (int n = 0; n < kD / 8; ++n) of[n][0] = of[n][1] = of[n][2] = of[n][3] = 0.f;
+  float mA = -INFINITY, mB = -INFINITY, lA = 0.f, lB = 0.f;
+  const uint32_t q_base = static_cast<uint32_t>(__cvta_generic_to_shared(sQ));
+
+  for (int c = 0; c < nchunks; ++c) {
+    const int buf = c & 1;
+    if (c + 1 < nchunks) {
+      load_chunk(c + 1, buf ^ 1);
+      cp_async_commit();
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();  // chunk c (and Q) visible to every warp
+    if (c == 0) {
+#pragma unroll
+      for (int ks = 0; ks < kD / 16; ++ks)
+        ldsm_x4(q_base + 2 * ((warp * 16 + (mi & 1) * 8 + ri) * kRow + ks * 16 + (mi >> 1) * 8), qa[ks]);
+    }
+    const uint32_t k_base = static_cast<uint32_t>(__cvta_generic_to_shared(sKV + buf * 2 * 64 * kRow));
+    const uint32_t v_base = k_base + 2 * 64 * kRow;
+
+    float sf[8][4];
+#pragma unroll
+    for (int n = 0; n < 8; ++n) sf[n][0] = sf[n][1] = sf[n][2] = sf[n][3] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < kD / 16; ++ks) {
+#pragma unroll
+      for (int nk = 0; nk < 4; ++nk) {
+        uint32_t bk[4];
+        ldsm_x4(k_base + 2 * ((nk * 16 + (mi >> 1) * 8 + ri) * kRow + ks * 16 + (mi & 1) * 8), bk);
+        mma16816<kBf16>(sf[2 * nk], qa[ks], bk[0], bk[1]);
+        mma16816<kBf16>(sf[2 * nk + 1], qa[ks], bk[2], bk[3]);
+      }
+    }
+    float cA = -INFINITY, cB = -INFINITY;
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int key = c * 64 + 8 * n + 2 * t4 + (e & 1);
+        const int row = e < 2 ? rowA : rowB;
+        const bool masked = key >= Skv || (causal && key > row);
+        sf[n][e] = masked ? -INFINITY : sf[n][e] * scale_log2;
+      }
+      cA = fmaxf(cA, fmaxf(sf[n][0], sf[n][1]));
+      cB = fmaxf(cB, fmaxf(sf[n][2], sf[n][3]));
+    }
+    cA = fmaxf(cA, __shfl_xor_sync(0xffffffffu, cA, 1));
+    cA = fmaxf(cA, __shfl_xor_sync(0xffffffffu, cA, 2));
+    cB = fmaxf(cB, __shfl_xor_sync(0xffffffffu, cB, 1));
+    cB = fmaxf(cB, __shfl_xor_sync(0xffffffffu, cB, 2));
+    const float nA = fmaxf(mA, cA), nB = fmaxf(mB, cB);
+    // A row with every key so far masked keeps m = -inf; its P is 0.
+    const float rA = nA == -INFINITY ? 0.f : nA, rB = nB == -INFINITY ? 0.f : nB;
+    const float aA = exp2f(mA - rA), aB = exp2f(mB - rB);  // m = -inf gives 0
+    mA = nA;
+    mB = nB;
+    lA *= aA;
+    lB *= aB;
+#pragma unroll
+    for (int n = 0; n < kD / 8; ++n) {
+      of[n][0] *= aA;
+      of[n][1] *= aA;
+      of[n][2] *= aB;
+      of[n][3] *= aB;
+    }
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+      sf[n][0] = exp2f(sf[n][0] - rA);
+      sf[n][1] = exp2f(sf[n][1] - rA);
+      sf[n][2] = exp2f(sf[n][2] - rB);
+      sf[n][3] = exp2f(sf[n][3] - rB);
+      lA += sf[n][0] + sf[n][1];
+      lB += sf[n][2] + sf[n][3];
+    }
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      const uint32_t a[4] = {pack16x2<kBf16>(sf[2 * kk][0], sf[2 * kk][1]),
+                             pack16x2<kBf16>(sf[2 * kk][2], sf[2 * kk][3]),
+                             pack16x2<kBf16>(sf[2 * kk + 1][0], sf[2 * kk + 1][1]),
+                             pack16x2<kBf16>(sf[2 * kk + 1][2], sf[2 * kk + 1][3])};
+#pragma unroll
+      for (int dt = 0; dt < kD / 8; dt += 2) {
+        uint32_t bv[4];
+        ldsm_x4_trans(v_base + 2 * ((kk * 16 + (mi & 1) * 8 + ri) * kRow + (dt + (mi >> 1)) * 8), bv);
+        mma16816<kBf16>(of[dt], a, bv[0], bv[1]);
+        mma16816<kBf16>(of[dt + 1], a, bv[2], bv[3]);
+      }
+    }
+    __syncthreads();  // every warp is done with this buffer before chunk c + 2 overwrites it
+  }
+
+  lA += __shfl_xor_sync(0xffffffffu, lA, 1);
+  lA += __shfl_xor_sync(0xffffffffu, lA, 2);
+  lB += __shfl_xor_sync(0xffffffffu, lB, 1);
+  lB += __shfl_xor_sync(0xffffffffu, lB, 2);
+  const float iA = lA > 0.f ? 1.f / lA : 0.f, iB = lB > 0.f ? 1.f / lB : 0.f;
+  uint16_t* ob = o + static_cast<size_t>(bh) * Sq * kD;
+#pragma unroll
+  for (int n = 0; n < kD / 8; ++n) {
+    const int col = 8 * n + 2 * t4;
+    if (rowA < Sq) *reinterpret_cast<uint32_t*>(ob + static_cast<size_t>(rowA) * kD + col) = pack16x2<kBf16>(of[n][0] * iA, of[n][1] * iA);
+    if (rowB < Sq) *reinterpret_cast<uint32_t*>(ob + static_cast<size_t>(rowB) * kD + col) = pack16x2<kBf16>(of[n][2] * iB, of[n][3] * iB);
+  }
+}
+
+template <bool kBf16, int kD>
+int launch_mid_typed(const void* q, const void* k, const void* v, void* out, bool causal, int BH, int H, int Sq,
+                     int Skv, float scale_log2, const GeneralStrides& st, cudaStream_t stream) {
+  const int smem = 5 * 64 * (kD + 8) * 2;  // Q + two buffers of K and V
+  auto kern = attn_mid_mma_kernel<kBf16, kD>;
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return -1;
+  const long long grid = static_cast<long long>(BH) * ((Sq + 63) / 64);
+  if (grid > 0x7fffffffLL) return -1;
+  kern<<<static_cast<unsigned>(grid), kMidWarps * 32, smem, stream>>>(
+      static_cast<const uint16_t*>(q), static_cast<const uint16_t*>(k), static_cast<const uint16_t*>(v),
+      static_cast<uint16_t*>(out), causal, H, Sq, Skv, scale_log2, st);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+template <bool kBf16>
+int launch_mid(const void* q, const void* k, const void* v, void* out, bool causal, int BH, int H, int Sq, int Skv,
+               int D, float sl, const GeneralStrides& st, cudaStream_t stream) {
+  switch (D) {
+    case 16: return launch_mid_typed<kBf16, 16>(q, k, v, out, causal, BH, H, Sq, Skv, sl, st, stream);
+    case 32: return launch_mid_typed<kBf16, 32>(q, k, v, out, causal, BH, H, Sq, Skv, sl, st, stream);
+    case 64: return launch_mid_typed<kBf16, 64>(q, k, v, out, causal, BH, H, Sq, Skv, sl, st, stream);
+    default: return launch_mid_typed<kBf16, 128>(q, k, v, out, causal, BH, H, Sq, Skv, sl, st, stream);
+  }
+}
+
 }  // namespace
+
+bool mid_kernel_takes(int Sq, int Skv, int D, int dtype) {
+  if (dtype == 2 || Sq < 1 || Skv < 1) return false;
+  // D = 16 / 32 have no tcgen05 path: this kernel at every length.  D = 64:
+  // where 256-row tcgen05 tiles are mostly padding (measured: up to 48 %
+  // faster for 40-160 query rows with up to 256 keys, and for 40 rows with
+  // 351; slower for 160 rows with 351 keys).  D = 128: the tcgen05 kernel.
+  if (D == 16 || D == 32) return true;
+  if (D == 64) return Sq <= kMidMaxQueries && (Sq <= 64 || Skv <= 256);
+  return false;
+}
+
+int launch_attn_mid(const void* q, const void* k, const void* v, void* out, int B, int H, int Sq, int Skv, int D,
+                    bool causal, float scale, int dtype, const GeneralStrides& st, cudaStream_t stream) {
+  const long long BH = static_cast<long long>(B) * H;
+  if (B <= 0 || H <= 0 || BH > 0x7fffffffLL || !mid_kernel_takes(Sq, Skv, D, dtype)) return -1;
+  auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  for (const long long* s3 : {st.q, st.k, st.v})
+    for (int i = 0; i < 3; ++i)
+      if ((s3[i] * 2) % 16 != 0) return -2;
+  if (!a16(q) || !a16(k) || !a16(v) || !a16(out)) return -2;
+  const float sl = scale * 1.4426950408889634f;
+  return dtype == 1 ? launch_mid<true>(q, k, v, out, causal, static_cast<int>(BH), H, Sq, Skv, D, sl, st, stream)
+                    : launch_mid<false>(q, k, v, out, causal, static_cast<int>(BH), H, Sq, Skv, D, sl, st, stream);
+}
 
 bool small_kernel_takes(int Sq, int Skv, int D, int dtype) {
   (void)dtype;

@@ -776,10 +776,16 @@ extern "C" int launch_attn_forward_strided(const void* q, const void* k, const v
   };
   // Short sequences (a few dozen rows per head): one warp per (batch, head)
   // slice instead of a mostly empty 256-row tile.
-  if (small_kernel_takes(Sq, Skv, D, static_cast<int>(dtype)))
-    return launch_attn_small(q, k, v, out, B, H, Sq, Skv, D, causal, scale, static_cast<int>(dtype), gs, stream) == 0
-               ? ATTN_OK
-               : ATTN_ERR_LAUNCH;
+  if (small_kernel_takes(Sq, Skv, D, static_cast<int>(dtype))) {
+    const int r = launch_attn_small(q, k, v, out, B, H, Sq, Skv, D, causal, scale, static_cast<int>(dtype), gs, stream);
+    if (r != -2) return r == 0 ? ATTN_OK : ATTN_ERR_LAUNCH;  // -2: rows not 16-byte aligned, run the general kernel
+  }
+  // Mid-length sequences (a few hundred rows per head): 64-row warp-level
+  // tensor-core tiles instead of 256-row tcgen05 tiles.
+  if (mid_kernel_takes(Sq, Skv, D, static_cast<int>(dtype))) {
+    const int r = launch_attn_mid(q, k, v, out, B, H, Sq, Skv, D, causal, scale, static_cast<int>(dtype), gs, stream);
+    if (r != -2) return r == 0 ? ATTN_OK : ATTN_ERR_LAUNCH;
+  }
   // The tensor-core kernel takes fp16/bf16 with D in {64, 128} and buffers
   // TMA can describe (16-byte aligned base and strides); every other call
   // runs the general kernel.

@@ -48,8 +48,9 @@ def _make(layout, shape, dtype, seed):
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("D", [64, 128])
 @pytest.mark.parametrize("layout", LAYOUTS)
-def test_tensor_core_strided(attn, layout, D, dtype):
-    qd, kd, vd = _make(layout, Shape(2, 3, 300, 300, D), dtype, seed=D)
+@pytest.mark.parametrize("L", [300, 200])  # tcgen05 kernel, 64-row warp-level kernel
+def test_tensor_core_strided(attn, layout, D, dtype, L):
+    qd, kd, vd = _make(layout, Shape(2, 3, L, L, D), dtype, seed=D)
     assert not qd.is_contiguous()
     for causal in (False, True):
         _ref_check(attn, qd, kd, vd, causal)
