@@ -1,22 +1,33 @@
-// General attention forward for the shapes the tensor-core kernel does not
-// take: fp32 inputs, head dims other than 64 and 128 (1..256), and fp16/bf16
-// pointers that are not 16-byte aligned (TMA needs aligned bases).
+// The attention kernels for the calls the tcgen05 kernel does not take well
+// (dispatch in attn_kernel.cu, launch_attn_forward_strided):
+//   attn_small_mma_kernel  fp16/bf16, <= 16 queries, <= 64 keys: one warp per
+//                          (batch, head) slice on warp-level tensor cores;
+//   attn_mid_mma_kernel    fp16/bf16 at D = 16 / 32 and short D = 64: 64-row
+//                          FlashAttention-2-style tiles on warp-level tensor
+//                          cores, K/V streamed in 64-key chunks;
+//   attn_small_kernel      <= 32 queries, <= 64 keys in any dtype: one warp per
+//                          slice, SIMT fp32;
+//   attn_general_kernel    everything else: fp32 inputs, head dims 1..256,
+//                          buffers TMA cannot describe.
 //
-// Covers the reference's remaining kernels on this path: the fp32 and
-// D=16 fp16 routes of its launcher (src/attn_kernel_torch.cu:625-689, the
-// simple kernel :36-97 and the WMMA D=16 kernel :356-621).  The math is the
-// reference's: s = (q . k) * scale, masked when causal and key > query
-// (top-left, src/attn_kernel_torch.cu:54,263), softmax in base 2 with a
-// running fp32 max and sum (:269-298), O = P V / sum (:333-354), and a row
-// with no unmasked key gives 0 (:335-336).
+// Together they cover the reference's remaining kernels on this path: the
+// fp32 and D=16 fp16 routes of its launcher (src/attn_kernel_torch.cu:625-689,
+// the simple kernel :36-97 and the WMMA D=16 kernel :356-621).  The math is
+// the reference's: s = (q . k) * scale, masked when causal and key > query
+// (top-left, src/attn_kernel_torch.cu:54,263), softmax in base 2 with an fp32
+// running max and sum (:269-298), O = P V / sum (:333-354), and a row with no
+// unmasked key gives 0 (:335-336).  Every accumulation is fp32; the
+// warp-level tensor-core kernels round P to the input type for P V, as the
+// tcgen05 kernel does.
 //
 // Layout: q [B, H, Sq, D], k/v [B, H, Skv, D] with any (batch, head, row)
 // strides and a contiguous head dim; o [B, H, Sq, D] contiguous.
-// CTA: 64 query rows of one (batch, head) and 256 threads, four per row;
-// thread t4 of a row owns the dims d = t4 + 4 i, so the four threads of a row
-// read four consecutive shared-memory banks.  Keys are staged in blocks of 32
-// (16 when D > 128) as fp32, zero beyond D; a row's four partial dot products
-// are summed with two butterfly shuffles.  Every accumulation is fp32.
+//
+// attn_general_kernel: 64 query rows of one (batch, head) per CTA and 256
+// threads, four per row; thread t4 of a row owns the dims d = t4 + 4 i, so the
+// four threads of a row read four consecutive shared-memory banks.  Keys are
+// staged in blocks of 32 (16 when D > 128) as fp32, zero beyond D; a row's
+// four partial dot products are summed with two butterfly shuffles.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -367,6 +378,18 @@ int launch_small_keys(const void* q, const void* k, const void* v, void* out, in
 // ---------------------------------------------------------------------------
 constexpr int kMmaWarps = 4;
 
+// 16-byte global -> shared copy that does not block the thread; with
+// valid = false nothing is read and the 16 bytes are zero-filled.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
@@ -429,25 +452,33 @@ __global__ void __launch_bounds__(kMmaWarps * 32) attn_small_mma_kernel(const ui
     const uint16_t* kp = k + b * st.k[0] + h * st.k[1];
     const uint16_t* vp = v + b * st.v[0] + h * st.v[1];
     __syncwarp();  // the previous slice's staging is no longer read
-    // Stage Q (16 rows) and K, V (kKeys rows) in 16-byte chunks, zero past Sq / Skv.
+    // Stage Q (16 rows) and K, V (kKeys rows) with 16-byte asynchronous
+    // copies, all in flight at once, zero-filled past Sq / Skv.
+#pragma unroll
     for (int e = lane; e < (16 + 2 * kKeys) * kChunks; e += 32) {
       const int r = e / kChunks, c = (e - r * kChunks) * 8;
-      uint4 val = make_uint4(0, 0, 0, 0);
+      const uint16_t* src;
       uint16_t* dst;
+      bool in;
       if (r < 16) {
-        if (r < Sq) val = __ldg(reinterpret_cast<const uint4*>(qp + r * st.q[2] + c));
+        in = r < Sq;
+        src = qp + (in ? r : 0) * st.q[2] + c;
         dst = sQ + r * kRow + c;
       } else if (r < 16 + kKeys) {
         const int key = r - 16;
-        if (key < Skv) val = __ldg(reinterpret_cast<const uint4*>(kp + key * st.k[2] + c));
+        in = key < Skv;
+        src = kp + (in ? key : 0) * st.k[2] + c;
         dst = sK + key * kRow + c;
       } else {
         const int key = r - 16 - kKeys;
-        if (key < Skv) val = __ldg(reinterpret_cast<const uint4*>(vp + key * st.v[2] + c));
+        in = key < Skv;
+        src = vp + (in ? key : 0) * st.v[2] + c;
         dst = sV + key * kRow + c;
       }
-      *reinterpret_cast<uint4*>(dst) = val;
+      cp_async16(static_cast<uint32_t>(__cvta_generic_to_shared(dst)), src, in);
     }
+    cp_async_commit();
+    cp_async_wait<0>();
     __syncwarp();
 
     // S = Q K^T: 2 * kNK n8 tiles of keys, kD / 16 k-steps over the head dim.
@@ -586,15 +617,6 @@ int launch_small_mma(const void* q, const void* k, const void* v, void* out, boo
 // ---------------------------------------------------------------------------
 constexpr int kMidWarps = 4;  // 64 query rows per CTA
 
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
 
 template <bool kBf16, int kD>
 __global__ void __launch_bounds__(kMidWarps * 32) attn_mid_mma_kernel(const uint16_t* __restrict__ q,
@@ -808,9 +830,10 @@ int launch_attn_mid(const void* q, const void* k, const void* v, void* out, int 
 }
 
 bool small_kernel_takes(int Sq, int Skv, int D, int dtype) {
-  (void)dtype;
   if (D != 16 && D != 32 && D != 64 && D != 128) return false;
-  return Sq >= 1 && Sq <= 32 / small_lanes_per_row(D) && Skv >= 1 && Skv <= kSmallMaxKeys;
+  if (Sq < 1 || Skv < 1 || Skv > kSmallMaxKeys) return false;
+  if (dtype != 2 && Sq <= 16) return true;  // warp-level tensor-core kernel: one m16 tile
+  return Sq <= 32 / small_lanes_per_row(D);  // SIMT kernel: one lane group per row
 }
 
 int launch_attn_small(const void* q, const void* k, const void* v, void* out, int B, int H, int Sq, int Skv, int D,

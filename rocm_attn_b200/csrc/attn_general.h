@@ -24,9 +24,10 @@ int launch_attn_general(const void* q, const void* k, const void* v, void* out, 
                         int D, bool causal, float scale, int dtype, const GeneralStrides& strides,
                         cudaStream_t stream);
 
-// Bounds of the short-sequence kernel (one warp per (batch, head) slice with
-// the slice's K and V in shared memory as fp32): D in {16, 32, 64, 128}, Skv
-// <= kSmallMaxKeys, Sq <= 32 rows at D <= 32, 16 at D = 64, 8 at D = 128.
+// Bounds of the short-sequence kernels (one warp per (batch, head) slice): D
+// in {16, 32, 64, 128}, Skv <= kSmallMaxKeys, and Sq <= 16 for fp16/bf16
+// (warp-level tensor cores) or, for the SIMT kernel, Sq <= 32 rows at D <= 32,
+// 16 at D = 64, 8 at D = 128.
 constexpr int kSmallMaxKeys = 64;
 
 // True when launch_attn_small takes a problem of these sizes.

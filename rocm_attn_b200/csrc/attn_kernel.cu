@@ -1,7 +1,9 @@
 // Fused attention forward for NVIDIA B200 (sm_100a): TMA -> shared memory ->
-// tcgen05 UMMA with accumulators in tensor memory, online softmax in base 2.
+// tcgen05 UMMA with accumulators in tensor memory, online softmax in base 2;
+// and the C-ABI entry points, whose dispatcher sends short, mid-length, fp32
+// and other-head-dim calls to the kernels of attn_general.cu.
 //
-// Replaces the reference's three HIP kernels and their launcher
+// Replaces the reference's HIP kernels and their launcher
 // (src/attn_kernel_torch.cu:36-689, src/attn_kernel.hip.cpp:36-367 of
 // JoursBleu/rocm_attn).  The math is the reference's: per query row,
 // s_j = (q . k_j) * scale, masked when causal and j > i
@@ -14,14 +16,18 @@
 //   warps 0-3  softmax of Q tile 0 (thread <-> TMEM lane <-> query row)
 //   warps 4-7  softmax of Q tile 1
 //   warp  8    UMMA issue (one elected lane) and TMEM allocation
-//   warp  9    TMA producer (Q once, then K/V blocks of 128 keys)
+//   warp  9    TMA producer for K/V blocks 1.. of 128 keys (thread 0 starts
+//              both Q tiles and block 0 during setup)
 // Tensor memory (512 columns x 128 lanes x 32 bit):
 //   S0 [0,128)  S1 [128,256)   fp32 scores of the current key block
-//   P0 = S0 cols [0,64), P1 = S1 cols [0,64)   16-bit probabilities (aliases S)
-//   O0 [256,256+D)  O1 [256+D,256+2D)          fp32 output accumulators
-// UMMA issue order per key block j (tcgen05.mma executes in issue order):
+//   D=128: P0 = S0 cols [0,64), P1 = S1 cols [0,64) (16-bit, aliasing S);
+//          O0 [256,384)  O1 [384,512) fp32 output accumulators
+//   D=64:  P0 [256,320)  P1 [320,384) apart from S; O0 [384,448) O1 [448,512)
+// UMMA issue order per key block j at D=128 (tcgen05.mma executes in issue
+// order):
 //   S0(j)=Q0 K_j^T, O1+=P1(j-1) V_{j-1}, S1(j)=Q1 K_j^T, O0+=P0(j) V_j
-// so each softmax warpgroup works while the tensor core runs the other tile.
+// so each softmax warpgroup works while the tensor core runs the other tile;
+// at D=64, S(j+1) is issued as soon as the softmax has read S(j).
 // The running max is only moved (and O rescaled) when it grows by more than
 // 2^8 in the exp2 domain; P values stay <= 256, exact in fp16/bf16 range, and
 // the final division by the matching running sum makes the result identical
