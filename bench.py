@@ -51,6 +51,7 @@ from rocm_attn_b200.workloads import (DTYPES, WORKLOADS, Shape, Workload, make_q
 
 METRIC = "attention fwd ms/iter and TFLOPS (% of B200 fp16 TC peak) at 1/2/4/8 GPUs"
 SPEC_DENSE_FP16_TFLOPS = 2250.0
+FALLBACK_HBM_GBS = 6650.0  # earlier measurement on this pool, used without MEASURED_PEAKS.json
 FALLBACK_PEAK_TFLOPS = 1590.0
 L2_FLUSH_BYTES = 256 << 20
 
@@ -87,6 +88,16 @@ def measured_peaks():
         return float(d["bf16_tflops"]), float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), "measured"
     except Exception:
         return FALLBACK_PEAK_TFLOPS, FALLBACK_PEAK_TFLOPS, "fallback"
+
+
+def measured_hbm_gbs():
+    """Measured HBM copy bandwidth (GB/s) and whether it was measured."""
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
 
 
 def profiled_traffic(workload_key: str, rank_heads: int, total_heads: int):
@@ -316,11 +327,20 @@ def run_ours(args, rank, world, local_rank):
     burst, sustained, peak_kind = measured_peaks()
     traffic = profiled_traffic(args.workload, local_heads, sum(s.bh for s in w.shapes)) if len(w.shapes) == 1 \
         else None
-    roofline = {"bound": "tensor", "achieved": round(kernel_tflops, 2), "peak": burst, "unit": "TFLOP/s",
-                "frac": round(kernel_tflops / burst, 4), "peak_kind": f"{peak_kind} bf16 dense GEMM (burst)",
-                "frac_of_spec_2250": round(kernel_tflops / SPEC_DENSE_FP16_TFLOPS, 4),
-                "traffic": traffic,
-                "algorithmic_bytes": sum(s.io_bytes() * len(r) / s.bh for s, r in shards)}
+    local_bytes = sum(s.io_bytes() * len(r) / s.bh for s, r in shards)
+    hbm, hbm_kind = measured_hbm_gbs()
+    if local_flops / max(local_bytes, 1.0) >= burst * 1e12 / (hbm * 1e9):
+        # arithmetic intensity above the ridge: bound by the tensor cores
+        roofline = {"bound": "tensor", "achieved": round(kernel_tflops, 2), "peak": burst, "unit": "TFLOP/s",
+                    "frac": round(kernel_tflops / burst, 4), "peak_kind": f"{peak_kind} bf16 dense GEMM (burst)",
+                    "frac_of_spec_2250": round(kernel_tflops / SPEC_DENSE_FP16_TFLOPS, 4)}
+    else:
+        # below the ridge (e.g. the UnifoLM short-sequence set): bound by HBM
+        gbs = local_bytes / (statistics.mean(step_ms) * 1e-3) / 1e9
+        roofline = {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+                    "frac": round(gbs / hbm, 4), "peak_kind": f"{hbm_kind} HBM copy bandwidth"}
+    roofline.update({"traffic": traffic, "algorithmic_bytes": local_bytes,
+                     "algorithmic_flops": local_flops})
 
     # ---- end to end through the public API with pinned host buffers
     e2e = None
