@@ -807,11 +807,11 @@ int launch_mid(const void* q, const void* k, const void* v, void* out, bool caus
 bool mid_kernel_takes(int Sq, int Skv, int D, int dtype) {
   if (dtype == 2 || Sq < 1 || Skv < 1) return false;
   // D = 16 / 32 have no tcgen05 path: this kernel at every length.  D = 64:
-  // where 256-row tcgen05 tiles are mostly padding (measured: up to 48 %
-  // faster for 40-160 query rows with up to 256 keys, and for 40 rows with
-  // 351; slower for 160 rows with 351 keys).  D = 128: the tcgen05 kernel.
+  // where the 128-row tcgen05 tiles are mostly padding (measured: 20-40 %
+  // faster for 40-64 query rows with up to 93 keys, even at 256 keys; slower
+  // from 128 query rows or 351 keys on).  D = 128: the tcgen05 kernel.
   if (D == 16 || D == 32) return true;
-  if (D == 64) return Sq <= kMidMaxQueries && (Sq <= 64 || Skv <= 256);
+  if (D == 64) return Sq <= kMidMaxQueries && Skv <= kMidMaxKeys;
   return false;
 }
 

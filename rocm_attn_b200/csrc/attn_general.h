@@ -41,11 +41,12 @@ int launch_attn_small(const void* q, const void* k, const void* v, void* out, in
 
 // Mid-length sequences on warp-level tensor cores (fp16/bf16, 16-byte aligned
 // rows): every D = 16 / 32 problem, and D = 64 with Sq <= kMidMaxQueries and
-// (Sq <= 64 or Skv <= 256).
+// Skv <= kMidMaxKeys.
 #ifndef RA_MID_MAX_QUERIES
-#define RA_MID_MAX_QUERIES 256
+#define RA_MID_MAX_QUERIES 64
 #endif
 constexpr int kMidMaxQueries = RA_MID_MAX_QUERIES;
+constexpr int kMidMaxKeys = 256;
 bool mid_kernel_takes(int Sq, int Skv, int D, int dtype);
 int launch_attn_mid(const void* q, const void* k, const void* v, void* out, int B, int H, int Sq, int Skv, int D,
                     bool causal, float scale, int dtype, const GeneralStrides& strides, cudaStream_t stream);

@@ -11,23 +11,25 @@
 // running fp32 max and sum (src/attn_kernel_torch.cu:269-298), O = P V / sum
 // (src/attn_kernel_torch.cu:333-354).
 //
-// CTA work unit: 256 query rows of one (batch, head) as two 128-row Q tiles.
-// Warp roles (320 threads):
+// CTA work unit.  D=128: 256 query rows of one (batch, head) as two 128-row
+// Q tiles, one CTA per SM.  D=64: one 128-row tile, two CTAs per SM.
+// Warp roles (320 threads with two tiles, 192 with one):
 //   warps 0-3  softmax of Q tile 0 (thread <-> TMEM lane <-> query row)
-//   warps 4-7  softmax of Q tile 1
-//   warp  8    UMMA issue (one elected lane) and TMEM allocation
-//   warp  9    TMA producer for K/V blocks 1.. of 128 keys (thread 0 starts
-//              both Q tiles and block 0 during setup)
-// Tensor memory (512 columns x 128 lanes x 32 bit):
-//   S0 [0,128)  S1 [128,256)   fp32 scores of the current key block
-//   D=128: P0 = S0 cols [0,64), P1 = S1 cols [0,64) (16-bit, aliasing S);
-//          O0 [256,384)  O1 [384,512) fp32 output accumulators
-//   D=64:  P0 [256,320)  P1 [320,384) apart from S; O0 [384,448) O1 [448,512)
+//   warps 4-7  softmax of Q tile 1 (two-tile CTAs)
+//   next warp  UMMA issue (one elected lane) and TMEM allocation
+//   last warp  TMA producer for K/V blocks 1.. of 128 keys (thread 0 starts
+//              the Q tiles and block 0 during setup)
+// Tensor memory (128 lanes x 32 bit; 512 columns for two tiles, 256 for one):
+//   D=128: S0 [0,128) S1 [128,256) fp32 scores of the current key block;
+//          P0 = S0 cols [0,64), P1 = S1 cols [0,64) (16-bit, aliasing S);
+//          O0 [256,384) O1 [384,512) fp32 output accumulators
+//   D=64:  S [0,128), P [128,192) apart from S, O [192,256)
 // UMMA issue order per key block j at D=128 (tcgen05.mma executes in issue
 // order):
 //   S0(j)=Q0 K_j^T, O1+=P1(j-1) V_{j-1}, S1(j)=Q1 K_j^T, O0+=P0(j) V_j
 // so each softmax warpgroup works while the tensor core runs the other tile;
-// at D=64, S(j+1) is issued as soon as the softmax has read S(j).
+// at D=64, S(j+1) is issued as soon as the softmax has read S(j), and the
+// other CTA on the SM keeps the tensor core busy meanwhile.
 // The running max is only moved (and O rescaled) when it grows by more than
 // 2^8 in the exp2 domain; P values stay <= 256, exact in fp16/bf16 range, and
 // the final division by the matching running sum makes the result identical
@@ -73,29 +75,37 @@ struct AttnParams {
   int Lk;           // key rows per (batch, head)
   int BH;           // batch * heads
   int H;            // heads (TMA coordinates are (d, row, head, batch))
-  int num_qblocks;  // ceil(Lq / 256)
+  int num_qblocks;  // ceil(Lq / query rows per CTA)
   int head_group;   // causal: heads per scheduling group (their K/V fit in L2)
   float scale_log2; // softmax scale * log2(e)
 };
 
-// Compile-time shape of the pipeline for head dimension kD.
-template <int kD>
+// Compile-time shape of the pipeline for head dimension kD and kTiles
+// 128-row Q tiles per CTA.
+template <int kD, int kTiles>
 struct Cfg {
-  static constexpr int kBM = 128;                       // rows per Q tile (2 tiles per CTA)
+  static_assert(kTiles == 1 || kTiles == 2, "one or two Q tiles per CTA");
+  static constexpr int kBM = 128;                       // rows per Q tile
   static constexpr int kBN = 128;                       // keys per block
-  static constexpr int kStagesK = kD == 128 ? 2 : 3;    // K ring depth
-  static constexpr int kStagesV = kD == 128 ? 2 : 3;    // V ring depth
+  static constexpr int kRows = kBM * kTiles;            // query rows per CTA
+  // K / V ring depths.  One-tile CTAs run two per SM, so each keeps to half
+  // of the SM's shared memory.
+  static constexpr int kStagesK = (kD == 128 || kTiles == 1) ? 2 : 3;
+  static constexpr int kStagesV = (kD == 128 || kTiles == 1) ? 2 : 3;
   static constexpr uint32_t kTileBytes = 128u * kD * 2; // one 128 x D tile
   static constexpr uint32_t kBlockBytes = 128u * 128;   // one 64-column block of a tile
-  static constexpr uint32_t kSmemBytes = 1024 + 2 * kTileBytes + (kStagesK + kStagesV) * kTileBytes;
-  static constexpr uint32_t kTmemCols = 512;
+  static constexpr uint32_t kSmemBytes = 1024 + kTiles * kTileBytes + (kStagesK + kStagesV) * kTileBytes;
+  static constexpr uint32_t kTmemCols = 256 * kTiles;
   // D=64 leaves TMEM room for P apart from S: the scores of block j+1 can
   // then be computed while the softmax of block j is still running.  At
   // D=128, P aliases the first half of S.
   static constexpr bool kSepP = kD == 64;
-  static constexpr uint32_t kColP = 256;                  // P0, P1 (64 columns each) when kSepP
-  static constexpr uint32_t kColO = kSepP ? 384 : 256;    // O0, O1
-  static constexpr int kThreads = 320;
+  static constexpr uint32_t kColP = 128 * kTiles;                        // P per tile (64 columns) when kSepP
+  static constexpr uint32_t kColO = kSepP ? 192 * kTiles : 128 * kTiles;  // O per tile (kD columns)
+  static constexpr int kMmaWarp = 4 * kTiles;            // after the softmax warpgroups
+  static constexpr int kTmaWarp = 4 * kTiles + 1;
+  static constexpr int kThreads = 128 * kTiles + 64;
+  static constexpr int kMinBlocksPerSm = 3 - kTiles;     // two one-tile CTAs share an SM
 };
 
 // Fraction of the softmax exponentials evaluated by the FMA-pipe polynomial
@@ -154,17 +164,17 @@ __device__ __forceinline__ void exp_pack32(const float (&s)[128], uint64_t c2, u
   }
 }
 
-template <bool kBf16, int kD, bool kCausal>
-__global__ void __launch_bounds__(320, 1)
+template <bool kBf16, int kD, bool kCausal, int kTiles>
+__global__ void __launch_bounds__(Cfg<kD, kTiles>::kThreads, Cfg<kD, kTiles>::kMinBlocksPerSm)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                     const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_o,
                     const AttnParams p) {
-  using C = Cfg<kD>;
+  using C = Cfg<kD, kTiles>;
   extern __shared__ uint8_t smem_raw[];
   __shared__ SharedCtl ctl;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;                                    // 2 tiles
-  uint8_t* sK = smem + 2 * C::kTileBytes;                // kStagesK tiles
+  uint8_t* sQ = smem;                                    // kTiles tiles
+  uint8_t* sK = smem + kTiles * C::kTileBytes;           // kStagesK tiles
   uint8_t* sV = sK + C::kStagesK * C::kTileBytes;        // kStagesV tiles
   volatile int* abort_flag = &ctl.abort_flag;
   int* status = &g_attn_status;
@@ -194,9 +204,9 @@ __global__ void __launch_bounds__(320, 1)
     qb = p.num_qblocks - 1 - static_cast<int>(blockIdx.x % p.num_qblocks);
   }
   const int hh = bh % p.H, bb = bh / p.H;  // TMA coordinates of the (batch, head) slice
-  const int q0 = qb * 256;
+  const int q0 = qb * C::kRows;
   const int n0 = tile_key_blocks(q0, 0, p.Lq, p.Lk, kCausal);
-  const int n1 = tile_key_blocks(q0, 1, p.Lq, p.Lk, kCausal);
+  const int n1 = kTiles > 1 ? tile_key_blocks(q0, 1, p.Lq, p.Lk, kCausal) : 0;
   const int nkb = max(n0, n1);
 
   if (threadIdx.x == 0) {
@@ -235,11 +245,11 @@ __global__ void __launch_bounds__(320, 1)
     for (int cb = 0; cb < kD / 64; ++cb)
       tma_load_4d(smem_addr(sV + cb * C::kBlockBytes), &map_v, &ctl.v_full[0], cb * 64, 0, hh, bb, pol_keep);
   }
-  if (warp == 8) {
+  if (warp == C::kMmaWarp) {
     tmem_alloc(smem_addr(&ctl.tmem_base), C::kTmemCols);
     tmem_relinquish();
   }
-  if (warp == 9 && lane == 0) {
+  if (warp == C::kTmaWarp && lane == 0) {
     tma_prefetch_desc(&map_q);
     tma_prefetch_desc(&map_k);
     tma_prefetch_desc(&map_v);
@@ -251,7 +261,7 @@ __global__ void __launch_bounds__(320, 1)
   const uint32_t tmem = ctl.tmem_base;
 
   RA_MARK(8190 - warp);
-  if (warp == 9) {
+  if (warp == C::kTmaWarp) {
     // ------------------------------------------------------------------ TMA
     const uint64_t pol_keep = l2_policy_evict_last();
     const bool leader = elect_one();
@@ -293,7 +303,7 @@ __global__ void __launch_bounds__(320, 1)
         if (last_v[s] >= 0) mbar_wait(&ctl.v_full[s], (last_v[s] / C::kStagesV) & 1, &no_abort, status, kWatchDrain);
       }
     }
-  } else if (warp == 8) {
+  } else if (warp == C::kMmaWarp) {
     // ------------------------------------------------------------------ UMMA
     const uint32_t idesc_s = umma_idesc_f16(kBf16, 128, 128, false);
     const uint32_t idesc_o = umma_idesc_f16(kBf16, 128, kD, true);
@@ -392,7 +402,6 @@ __global__ void __launch_bounds__(320, 1)
         RA_MARK(4096 + j * 8 + 1);
       }
     } else {
-    // Issue order per key block j: S0(j), O1 += P1(j-1) V(j-1), S1(j), O0 += P0(j) V(j).
     // Issue order per key block j: S0(j), O1 += P1(j-1) V(j-1), S1(j), O0 += P0(j) V(j).
     for (int j = 0; j < nkb && ok; ++j) {
       const int sk = j % C::kStagesK, sv = j % C::kStagesV;
@@ -649,7 +658,7 @@ __global__ void __launch_bounds__(320, 1)
   RA_MARK(8180 - warp);
   tc_fence_before();
   __syncthreads();
-  if (warp == 8) {
+  if (warp == C::kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, C::kTmemCols);
   }
@@ -669,10 +678,10 @@ struct Strides {
 // (the caller then runs the general kernel).
 constexpr int kNoTensorMap = -2;
 
-template <bool kBf16, int kD, bool kCausal>
+template <bool kBf16, int kD, bool kCausal, int kTiles>
 static int launch_impl(const void* q, const void* k, const void* v, void* out, int B, int H, int Sq, int Skv,
                        const Strides& sq, const Strides& sk, const Strides& sv, float scale, cudaStream_t stream) {
-  using C = Cfg<kD>;
+  using C = Cfg<kD, kTiles>;
   CUtensorMap mq, mk, mv, mo;
   const uint64_t D = kD;
   const int r[4] = {
@@ -686,7 +695,7 @@ static int launch_impl(const void* q, const void* k, const void* v, void* out, i
   for (int e : r)
     if (e != 0) return ATTN_ERR_TENSOR_MAP;
 
-  auto kern = attn_fwd_kernel<kBf16, kD, kCausal>;
+  auto kern = attn_fwd_kernel<kBf16, kD, kCausal, kTiles>;
   // Opt in to the large dynamic shared-memory carve-out once per device.
   static bool configured[64] = {};
   static std::mutex mu;
@@ -698,6 +707,11 @@ static int launch_impl(const void* q, const void* k, const void* v, void* out, i
       if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(C::kSmemBytes)) != cudaSuccess)
         return ATTN_ERR_LAUNCH;
+      // One-tile CTAs: ask for the largest shared-memory carve-out so two
+      // of them fit on an SM.
+      if (kTiles == 1 && cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                              static_cast<int>(cudaSharedmemCarveoutMaxShared)) != cudaSuccess)
+        return ATTN_ERR_LAUNCH;
       configured[dev] = true;
     }
   }
@@ -707,7 +721,7 @@ static int launch_impl(const void* q, const void* k, const void* v, void* out, i
   const int BH = B * H;
   prm.BH = BH;
   prm.H = H;
-  prm.num_qblocks = (Sq + 255) / 256;
+  prm.num_qblocks = (Sq + C::kRows - 1) / C::kRows;
   // K+V bytes of one head; about 48 MB of them (a third of L2) per group.
   const double kv_bytes = 2.0 * Skv * kD * 2;
   prm.head_group = static_cast<int>(fmax(1.0, fmin(static_cast<double>(BH), 48.0e6 / kv_bytes)));
@@ -717,6 +731,16 @@ static int launch_impl(const void* q, const void* k, const void* v, void* out, i
   kern<<<static_cast<unsigned>(grid), C::kThreads, C::kSmemBytes, stream>>>(mq, mk, mv, mo, prm);
   return cudaGetLastError() == cudaSuccess ? ATTN_OK : ATTN_ERR_LAUNCH;
 }
+
+// Q tiles per CTA.  D=64: one, and two CTAs per SM (the TMEM of one tile is
+// 256 columns: S, P and O), so one CTA's set-up, first block and epilogue
+// overlap the other's softmax.  D=128: two, one CTA per SM (two one-tile
+// CTAs would have to single-buffer their 32 KB K and V blocks to fit).
+#ifndef RA_D64_TILES
+#define RA_D64_TILES 1
+#endif
+constexpr int kD64Tiles = RA_D64_TILES;
+constexpr int kD128Tiles = 2;
 
 // Compute capability 10.x check, cached per device.
 static int check_device() {
@@ -800,7 +824,7 @@ extern "C" int launch_attn_forward_strided(const void* q, const void* k, const v
   int st = ATTN_ERR_UNSUPPORTED;
 #define RA_DISPATCH(BF, DD, CA)                                                           \
   if (bf16 == BF && D == DD && causal == CA)                                              \
-    st = launch_impl<BF, DD, CA>(q, k, v, out, B, H, Sq, Skv, sq, sk, sv, scale, stream); \
+    st = launch_impl<BF, DD, CA, DD == 64 ? kD64Tiles : kD128Tiles>(q, k, v, out, B, H, Sq, Skv, sq, sk, sv, scale, stream); \
   else
   RA_DISPATCH(false, 128, false)
   RA_DISPATCH(false, 128, true)
