@@ -35,9 +35,12 @@ SMALL = [
     Shape(1, 2, 128, 128, 64), Shape(1, 2, 128, 128, 128), Shape(1, 2, 256, 256, 128), Shape(2, 3, 300, 300, 64),
     Shape(1, 1, 1, 1, 64), Shape(1, 1, 1, 1, 128), Shape(1, 2, 17, 17, 128), Shape(1, 2, 129, 129, 64),
     Shape(1, 1, 257, 257, 128), Shape(2, 2, 384, 384, 128), Shape(3, 5, 513, 513, 64), Shape(1, 2, 640, 640, 128),
+    # D=64 around the 64-query mid-kernel limit and the 128-row tensor-core unit
+    Shape(1, 2, 65, 65, 64), Shape(1, 3, 255, 255, 64),
 ]
 CROSS = [Shape(1, 2, 6, 9, 64), Shape(1, 2, 100, 300, 64), Shape(1, 2, 300, 100, 128), Shape(2, 2, 256, 1000, 128),
-         Shape(1, 3, 1000, 256, 64), Shape(16, 5, 40, 93, 64), Shape(16, 4, 160, 351, 64)]
+         Shape(1, 3, 1000, 256, 64), Shape(16, 5, 40, 93, 64), Shape(16, 4, 160, 351, 64),
+         Shape(1, 2, 64, 257, 64), Shape(2, 2, 383, 129, 64), Shape(1, 2, 130, 1, 64)]
 
 
 @pytest.mark.parametrize("dtype", ["fp16", "bf16"])
