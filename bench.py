@@ -27,6 +27,8 @@ Reported on the line:
                 reference's _sdpa_fallback runs it) on the host cores, fp32,
                 on a bounded sample of the same workload's heads
   clocks        nvidia-smi samples taken during the timed region
+  gather        N > 1 only: the NCCL all-gather that assembles the full O
+                on every rank, timed on its own after the timed region
 ``--impl reference`` times that CPU reference path alone on the same
 workload (rank 0; other ranks exit without work).
 """
@@ -263,6 +265,39 @@ def run_reference_arm(args, rank, world):
 
 # ---------------------------------------------------------------- our arm
 
+def time_gather(w, shards, step, world, rank, dev, stream, reps: int = 5):
+    """Times ``sharding.gather_heads`` (NCCL all_gather_into_tensor of every
+    rank's O slices into the full [B, H, Lq, D] O) with CUDA events, max over
+    ranks.  Every rank makes the same collective calls in the same order."""
+    import torch.distributed as dist
+    from rocm_attn_b200.sharding import gather_heads
+
+    outs = iter(step())
+    local = []
+    for s, r in shards:
+        local.append(next(outs) if len(r) > 0 else
+                     torch.empty((1, 0, s.Lq, s.D), dtype=DTYPES[w.dtype], device=dev))
+    for (s, _), o in zip(shards, local):  # warm-up (communicator set-up)
+        gather_heads(o, s.B, s.H, world, rank)
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    g0.record(stream)
+    for _ in range(reps):
+        for (s, _), o in zip(shards, local):
+            gather_heads(o, s.B, s.H, world, rank)
+    g1.record(stream)
+    torch.cuda.synchronize(dev)
+    t = torch.tensor([g0.elapsed_time(g1) / reps], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    full_bytes = sum(2 * s.bh * s.Lq * s.D for s in w.shapes)
+    algbw = full_bytes / (ms * 1e-3) / 1e9
+    return {"collective": "NCCL all_gather_into_tensor of O (sharding.gather_heads)", "ms": round(ms, 4),
+            "bytes_gathered": int(full_bytes), "algbw_gbs": round(algbw, 1),
+            "busbw_gbs": round(algbw * (world - 1) / world, 1), "reps": reps}
+
+
 def run_ours(args, rank, world, local_rank):
     import rocm_attn_op  # public API (drop-in name)
 
@@ -342,6 +377,10 @@ def run_ours(args, rank, world, local_rank):
     roofline.update({"traffic": traffic, "algorithmic_bytes": local_bytes,
                      "algorithmic_flops": local_flops})
 
+    # ---- the all-gather that assembles the full O on every rank (N > 1 only;
+    # outside the timed region, reported on its own)
+    gather = time_gather(w, shards, step, world, rank, dev, stream) if dist else None
+
     # ---- end to end through the public API with pinned host buffers
     e2e = None
     if not args.no_e2e:
@@ -398,6 +437,7 @@ def run_ours(args, rank, world, local_rank):
                    "cuda_graph": bool(args.graph),
                    "frac_of_spec_dense_fp16": round(tflops / world / SPEC_DENSE_FP16_TFLOPS, 4)},
         "e2e": e2e,
+        "gather": gather,
         "gpu_launches": args.steps * sum(1 for _, r in shards if len(r) > 0),
         "roofline": roofline,
         "clocks": clocks,

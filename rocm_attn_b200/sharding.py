@@ -42,6 +42,8 @@ def gather_heads(o_local: torch.Tensor, B: int, H: int, world: int, rank: int,
         send = torch.cat([send, pad], 0)
     recv = torch.empty(world * n_max, L, D, dtype=o_local.dtype, device=o_local.device)
     dist.all_gather_into_tensor(recv, send.contiguous(), group=group)
+    if all(n == n_max for n in sizes):
+        return recv.view(B, H, L, D)  # equal shards land in order: no copy
     parts = [recv[r * n_max:r * n_max + sizes[r]] for r in range(world)]
     return torch.cat(parts, 0).view(B, H, L, D)
 

@@ -39,15 +39,20 @@ def _worker_gather(rank, world, port, q):
         from rocm_attn_b200.workloads import Shape, make_qkv
 
         dist = _init(rank, world, port)
-        shape = Shape(2, 3, 20, 24, 64)  # 6 slices over 2 ranks
-        qq, kk, vv = make_qkv(shape, torch.float32, seed=5)
-        full = sharded_forward(oracle.c_oracle_forward, qq, kk, vv, causal=True, world=world, rank=rank,
-                               gather=True)
-        ref = oracle.c_oracle_forward(qq, kk, vv, causal=True)
+        err = 0.0
+        # 6 slices over 2 ranks (equal shards: gathered in place) and 5 slices
+        # (3 + 2: padded for the collective, then reassembled)
+        for shape in (Shape(2, 3, 20, 24, 64), Shape(1, 5, 17, 9, 64)):
+            qq, kk, vv = make_qkv(shape, torch.float32, seed=5)
+            full = sharded_forward(oracle.c_oracle_forward, qq, kk, vv, causal=True, world=world, rank=rank,
+                                   gather=True)
+            ref = oracle.c_oracle_forward(qq, kk, vv, causal=True)
+            assert full.shape == ref.shape
+            err = max(err, oracle.max_abs_err(full, ref))
         # max-over-ranks reduction used for timing
         t = torch.tensor([float(rank + 1)])
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        q.put((rank, oracle.max_abs_err(full, ref), float(t.item())))
+        q.put((rank, err, float(t.item())))
         dist.destroy_process_group()
     except Exception:
         q.put((rank, "error", traceback.format_exc()))
