@@ -120,7 +120,7 @@ constexpr int kPolyNum = RA_POLY_NUM;
 constexpr int kPolyDen = RA_POLY_DEN;
 
 struct __align__(8) SharedCtl {
-  uint64_t q_full;
+  uint64_t q_full[2];     // [tile]: Q tile loaded
   uint64_t k_full[3], k_empty[3];
   uint64_t v_full[3], v_empty[3];
   uint64_t s_full[2];     // [tile]: S(j) computed
@@ -211,7 +211,8 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles>::kThreads, Cfg<kD, kTiles>::kM
 
   if (threadIdx.x == 0) {
     ctl.abort_flag = 0;
-    mbar_init(&ctl.q_full, 1);
+    mbar_init(&ctl.q_full[0], 1);
+    mbar_init(&ctl.q_full[1], 1);
     for (int s = 0; s < 3; ++s) {
       mbar_init(&ctl.k_full[s], 1);
       mbar_init(&ctl.k_empty[s], 1);
@@ -228,19 +229,23 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles>::kThreads, Cfg<kD, kTiles>::kM
     }
     mbar_init(&ctl.mma_done, 1);
     fence_mbar_init();
-    // Start the first copies (Q tiles, K and V of block 0) before the CTA
-    // synchronises and allocates tensor memory; the producer warp issues
-    // every later block.
+    // Start the first copies before the CTA synchronises and allocates
+    // tensor memory, in the order the first products need them (Q tile 0
+    // and K block 0 for S0(0), then Q tile 1, then V block 0); the producer
+    // warp issues every later block.
     const uint64_t pol_stream = l2_policy_evict_first();
     const uint64_t pol_keep = l2_policy_evict_last();
-    mbar_arrive_expect_tx(&ctl.q_full, (n1 > 0 ? 2u : 1u) * C::kTileBytes);
-    for (int t = 0; t < (n1 > 0 ? 2 : 1); ++t)
+    auto load_q = [&](int t) {
+      mbar_arrive_expect_tx(&ctl.q_full[t], C::kTileBytes);
       for (int cb = 0; cb < kD / 64; ++cb)
-        tma_load_4d(smem_addr(sQ + t * C::kTileBytes + cb * C::kBlockBytes), &map_q, &ctl.q_full, cb * 64,
+        tma_load_4d(smem_addr(sQ + t * C::kTileBytes + cb * C::kBlockBytes), &map_q, &ctl.q_full[t], cb * 64,
                     q0 + t * 128, hh, bb, pol_stream);
+    };
+    load_q(0);
     mbar_arrive_expect_tx(&ctl.k_full[0], C::kTileBytes);
     for (int cb = 0; cb < kD / 64; ++cb)
       tma_load_4d(smem_addr(sK + cb * C::kBlockBytes), &map_k, &ctl.k_full[0], cb * 64, 0, hh, bb, pol_keep);
+    if (n1 > 0) load_q(1);
     mbar_arrive_expect_tx(&ctl.v_full[0], C::kTileBytes);
     for (int cb = 0; cb < kD / 64; ++cb)
       tma_load_4d(smem_addr(sV + cb * C::kBlockBytes), &map_v, &ctl.v_full[0], cb * 64, 0, hh, bb, pol_keep);
@@ -297,7 +302,8 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles>::kThreads, Cfg<kD, kTiles>::kM
     if (!ok) {
       // Aborted: let every copy already issued land before the CTA exits.
       volatile int no_abort = 0;
-      mbar_wait(&ctl.q_full, 0, &no_abort, status, kWatchDrain);
+      mbar_wait(&ctl.q_full[0], 0, &no_abort, status, kWatchDrain);
+      if (n1 > 0) mbar_wait(&ctl.q_full[1], 0, &no_abort, status, kWatchDrain);
       for (int s = 0; s < 3; ++s) {
         if (last_k[s] >= 0) mbar_wait(&ctl.k_full[s], (last_k[s] / C::kStagesK) & 1, &no_abort, status, kWatchDrain);
         if (last_v[s] >= 0) mbar_wait(&ctl.v_full[s], (last_v[s] / C::kStagesV) & 1, &no_abort, status, kWatchDrain);
@@ -343,12 +349,13 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles>::kThreads, Cfg<kD, kTiles>::kM
       return true;
     };
 
-    bool ok = __all_sync(0xffffffffu, mbar_wait(&ctl.q_full, 0, abort_flag, status, kWatchQ + 2));
+    bool ok = __all_sync(0xffffffffu, mbar_wait(&ctl.q_full[0], 0, abort_flag, status, kWatchQ + 2));
     if constexpr (C::kSepP) {
       // Issue order: S0(0) S1(0) | per block j: S0(j+1) O0+=P0(j)V(j) S1(j+1) O1+=P1(j)V(j).
       // S(j+1) only waits for the softmax to have read S(j) (s_free), so the
       // scores of the next block are ready when the softmax finishes.
       const int nt[2] = {n0, n1};
+      if (ok && n1 > 0) ok = __all_sync(0xffffffffu, mbar_wait(&ctl.q_full[1], 0, abort_flag, status, kWatchQ + 3));
       if (ok) {
         ok = __all_sync(0xffffffffu, mbar_wait(&ctl.k_full[0], 0, abort_flag, status, kWatchK + 2));
         if (ok) {
@@ -425,6 +432,11 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles>::kThreads, Cfg<kD, kTiles>::kM
         __syncwarp();
       }
       RA_MARK(4096 + j * 8 + 2);
+      if (j == 0 && n1 > 0) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&ctl.q_full[1], 0, abort_flag, status, kWatchQ + 3));
+        if (!ok) break;
+        tc_fence_after();
+      }
       if (leader) {
         if (j < n1) {
           issue_s(tS1, q_addr1, k_addr);
