@@ -177,8 +177,8 @@ int launch_dims(const void* q, const void* k, const void* v, void* out, int BH, 
 // kPer * (l % kLpr + 1)), kLpr = 32 / (rows rounded up to a power of two).
 // With at most 64 keys a row keeps all its scores in registers: one max, one
 // exponential per key and one pass over V, with no running rescale.
-// This replaces a 256-row tensor-core tile per slice, which for the
-// reference's 16-row inference shapes would be 94% padding.
+// This replaces a 128- or 256-row tensor-core unit per slice, which for the
+// reference's 16-row inference shapes would be 88-94% padding.
 // ---------------------------------------------------------------------------
 constexpr int kSmallWarps = 4;
 

@@ -817,13 +817,14 @@ extern "C" int launch_attn_forward_strided(const void* q, const void* k, const v
                : ATTN_ERR_LAUNCH;
   };
   // Short sequences (a few dozen rows per head): one warp per (batch, head)
-  // slice instead of a mostly empty 256-row tile.
+  // slice instead of a mostly empty 128- or 256-row tcgen05 unit.
   if (small_kernel_takes(Sq, Skv, D, static_cast<int>(dtype))) {
     const int r = launch_attn_small(q, k, v, out, B, H, Sq, Skv, D, causal, scale, static_cast<int>(dtype), gs, stream);
     if (r != -2) return r == 0 ? ATTN_OK : ATTN_ERR_LAUNCH;  // -2: rows not 16-byte aligned, run the general kernel
   }
-  // Mid-length sequences (a few hundred rows per head): 64-row warp-level
-  // tensor-core tiles instead of 256-row tcgen05 tiles.
+  // D = 16 / 32 at any length, and D = 64 with at most 64 queries and 256
+  // keys: 64-row warp-level tensor-core tiles instead of 128-row tcgen05
+  // tiles.
   if (mid_kernel_takes(Sq, Skv, D, static_cast<int>(dtype))) {
     const int r = launch_attn_mid(q, k, v, out, B, H, Sq, Skv, D, causal, scale, static_cast<int>(dtype), gs, stream);
     if (r != -2) return r == 0 ? ATTN_OK : ATTN_ERR_LAUNCH;
