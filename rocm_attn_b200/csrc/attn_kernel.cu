@@ -80,32 +80,36 @@ struct AttnParams {
   float scale_log2; // softmax scale * log2(e)
 };
 
-// Compile-time shape of the pipeline for head dimension kD and kTiles
-// 128-row Q tiles per CTA.
-template <int kD, int kTiles>
+// Compile-time shape of the pipeline for head dimension kD, kTiles 128-row
+// Q tiles per CTA and kBlockKeys keys per K/V block.
+template <int kD, int kTiles, int kBlockKeys>
 struct Cfg {
   static_assert(kTiles == 1 || kTiles == 2, "one or two Q tiles per CTA");
+  static_assert(kBlockKeys == 128 || (kBlockKeys == 64 && kD == 64 && kTiles == 1),
+                "64-key blocks only for one-tile D=64 CTAs");
   static constexpr int kBM = 128;                       // rows per Q tile
-  static constexpr int kBN = 128;                       // keys per block
+  static constexpr int kBN = kBlockKeys;                // keys per block
   static constexpr int kRows = kBM * kTiles;            // query rows per CTA
-  // K / V ring depths.  One-tile CTAs run two per SM, so each keeps to half
-  // of the SM's shared memory.
-  static constexpr int kStagesK = (kD == 128 || kTiles == 1) ? 2 : 3;
-  static constexpr int kStagesV = (kD == 128 || kTiles == 1) ? 2 : 3;
-  static constexpr uint32_t kTileBytes = 128u * kD * 2; // one 128 x D tile
-  static constexpr uint32_t kBlockBytes = 128u * 128;   // one 64-column block of a tile
-  static constexpr uint32_t kSmemBytes = 1024 + kTiles * kTileBytes + (kStagesK + kStagesV) * kTileBytes;
-  static constexpr uint32_t kTmemCols = 256 * kTiles;
-  // D=64 leaves TMEM room for P apart from S: the scores of block j+1 can
-  // then be computed while the softmax of block j is still running.  At
-  // D=128, P aliases the first half of S.
-  static constexpr bool kSepP = kD == 64;
+  // K / V ring depths.  One-tile CTAs run two (three with 64-key blocks) per
+  // SM, so each keeps to its share of the SM's shared memory.
+  static constexpr int kStagesK = kBN == 64 ? 3 : (kD == 128 || kTiles == 1) ? 2 : 3;
+  static constexpr int kStagesV = kStagesK;
+  static constexpr uint32_t kTileBytes = 128u * kD * 2; // one 128 x D Q tile
+  static constexpr uint32_t kBlockBytes = 128u * 128;   // one 64-column block of a Q tile
+  static constexpr uint32_t kKVBytes = kBN * kD * 2u;   // one K or V block
+  static constexpr uint32_t kKVBlockBytes = kBN * 128u; // one 64-column block of a K or V block
+  static constexpr uint32_t kSmemBytes = 1024 + kTiles * kTileBytes + (kStagesK + kStagesV) * kKVBytes;
+  // D=64 with 128-key blocks leaves TMEM room for P apart from S: the scores
+  // of block j+1 can then be computed while the softmax of block j is still
+  // running.  Otherwise P aliases the first half of S.
+  static constexpr bool kSepP = kD == 64 && kBN == 128;
+  static constexpr uint32_t kTmemCols = kTiles == 2 ? 512 : (kBN == 64 ? 128 : 256);
   static constexpr uint32_t kColP = 128 * kTiles;                        // P per tile (64 columns) when kSepP
-  static constexpr uint32_t kColO = kSepP ? 192 * kTiles : 128 * kTiles;  // O per tile (kD columns)
+  static constexpr uint32_t kColO = kSepP ? 192 * kTiles : kBN * kTiles;  // O per tile (kD columns)
   static constexpr int kMmaWarp = 4 * kTiles;            // after the softmax warpgroups
   static constexpr int kTmaWarp = 4 * kTiles + 1;
   static constexpr int kThreads = 128 * kTiles + 64;
-  static constexpr int kMinBlocksPerSm = 3 - kTiles;     // two one-tile CTAs share an SM
+  static constexpr int kMinBlocksPerSm = kTiles == 2 ? 1 : (kBN == 64 ? 3 : 2);  // one-tile CTAs share an SM
 };
 
 // Fraction of the softmax exponentials evaluated by the FMA-pipe polynomial
@@ -133,21 +137,22 @@ struct __align__(8) SharedCtl {
   int abort_flag;
 };
 
-// Number of 128-key blocks Q tile `t` of the CTA starting at row q0 needs.
-__device__ __forceinline__ int tile_key_blocks(int q0, int t, int Lq, int Lk, bool causal) {
+// Number of bn-key blocks Q tile `t` of the CTA starting at row q0 needs.
+__device__ __forceinline__ int tile_key_blocks(int q0, int t, int Lq, int Lk, bool causal, int bn) {
   const int first = q0 + t * 128;
   if (first >= Lq) return 0;
-  const int all = (Lk + 127) / 128;
+  const int all = (Lk + bn - 1) / bn;
   if (!causal) return all;
   const int last = min(first + 127, Lq - 1);
-  return min(all, last / 128 + 1);
+  return min(all, last / bn + 1);
 }
 
 // exp2 of 32 consecutive scores (relative to the reference point -nmc2/c2),
 // packed to 16-bit pairs; returns the fp32 sum of the exponentials in `sum2`.
-template <bool kBf16, int kSrc, int kDst>
-__device__ __forceinline__ void exp_pack32(const float (&s)[128], uint64_t c2, uint64_t nmc2, uint32_t (&pk)[32],
+template <bool kBf16, int kSrc, int kDst, int kN>
+__device__ __forceinline__ void exp_pack32(const float (&s)[kN], uint64_t c2, uint64_t nmc2, uint32_t (&pk)[32],
                                            uint64_t& sum2) {
+  static_assert(kSrc + 32 <= kN && kDst + 16 <= 32, "source or destination out of range");
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
     const uint64_t x = f2_fma(f2(s[kSrc + 2 * i], s[kSrc + 2 * i + 1]), c2, nmc2);
@@ -164,18 +169,18 @@ __device__ __forceinline__ void exp_pack32(const float (&s)[128], uint64_t c2, u
   }
 }
 
-template <bool kBf16, int kD, bool kCausal, int kTiles>
-__global__ void __launch_bounds__(Cfg<kD, kTiles>::kThreads, Cfg<kD, kTiles>::kMinBlocksPerSm)
+template <bool kBf16, int kD, bool kCausal, int kTiles, int kBlockKeys>
+__global__ void __launch_bounds__(Cfg<kD, kTiles, kBlockKeys>::kThreads, Cfg<kD, kTiles, kBlockKeys>::kMinBlocksPerSm)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                     const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_o,
                     const AttnParams p) {
-  using C = Cfg<kD, kTiles>;
+  using C = Cfg<kD, kTiles, kBlockKeys>;
   extern __shared__ uint8_t smem_raw[];
   __shared__ SharedCtl ctl;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;                                    // kTiles tiles
-  uint8_t* sK = smem + kTiles * C::kTileBytes;           // kStagesK tiles
-  uint8_t* sV = sK + C::kStagesK * C::kTileBytes;        // kStagesV tiles
+  uint8_t* sK = smem + kTiles * C::kTileBytes;           // kStagesK blocks
+  uint8_t* sV = sK + C::kStagesK * C::kKVBytes;         // kStagesV blocks
   volatile int* abort_flag = &ctl.abort_flag;
   int* status = &g_attn_status;
 
@@ -205,8 +210,8 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles>::kThreads, Cfg<kD, kTiles>::kM
   }
   const int hh = bh % p.H, bb = bh / p.H;  // TMA coordinates of the (batch, head) slice
   const int q0 = qb * C::kRows;
-  const int n0 = tile_key_blocks(q0, 0, p.Lq, p.Lk, kCausal);
-  const int n1 = kTiles > 1 ? tile_key_blocks(q0, 1, p.Lq, p.Lk, kCausal) : 0;
+  const int n0 = tile_key_blocks(q0, 0, p.Lq, p.Lk, kCausal, C::kBN);
+  const int n1 = kTiles > 1 ? tile_key_blocks(q0, 1, p.Lq, p.Lk, kCausal, C::kBN) : 0;
   const int nkb = max(n0, n1);
 
   if (threadIdx.x == 0) {
@@ -242,13 +247,13 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles>::kThreads, Cfg<kD, kTiles>::kM
                     q0 + t * 128, hh, bb, pol_stream);
     };
     load_q(0);
-    mbar_arrive_expect_tx(&ctl.k_full[0], C::kTileBytes);
+    mbar_arrive_expect_tx(&ctl.k_full[0], C::kKVBytes);
     for (int cb = 0; cb < kD / 64; ++cb)
-      tma_load_4d(smem_addr(sK + cb * C::kBlockBytes), &map_k, &ctl.k_full[0], cb * 64, 0, hh, bb, pol_keep);
+      tma_load_4d(smem_addr(sK + cb * C::kKVBlockBytes), &map_k, &ctl.k_full[0], cb * 64, 0, hh, bb, pol_keep);
     if (n1 > 0) load_q(1);
-    mbar_arrive_expect_tx(&ctl.v_full[0], C::kTileBytes);
+    mbar_arrive_expect_tx(&ctl.v_full[0], C::kKVBytes);
     for (int cb = 0; cb < kD / 64; ++cb)
-      tma_load_4d(smem_addr(sV + cb * C::kBlockBytes), &map_v, &ctl.v_full[0], cb * 64, 0, hh, bb, pol_keep);
+      tma_load_4d(smem_addr(sV + cb * C::kKVBlockBytes), &map_v, &ctl.v_full[0], cb * 64, 0, hh, bb, pol_keep);
   }
   if (warp == C::kMmaWarp) {
     tmem_alloc(smem_addr(&ctl.tmem_base), C::kTmemCols);
@@ -279,10 +284,10 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles>::kThreads, Cfg<kD, kTiles>::kM
                       mbar_wait(&ctl.k_empty[sk], ((j / C::kStagesK) & 1) ^ 1, abort_flag, status, kWatchK + 1));
       if (!ok) break;
       if (leader) {
-        mbar_arrive_expect_tx(&ctl.k_full[sk], C::kTileBytes);
+        mbar_arrive_expect_tx(&ctl.k_full[sk], C::kKVBytes);
         for (int cb = 0; cb < kD / 64; ++cb)
-          tma_load_4d(smem_addr(sK + sk * C::kTileBytes + cb * C::kBlockBytes), &map_k, &ctl.k_full[sk], cb * 64,
-                      j * 128, hh, bb, pol_keep);
+          tma_load_4d(smem_addr(sK + sk * C::kKVBytes + cb * C::kKVBlockBytes), &map_k, &ctl.k_full[sk], cb * 64,
+                      j * C::kBN, hh, bb, pol_keep);
       }
       last_k[sk] = j;
       RA_MARK(6144 + j * 4 + 1);
@@ -291,10 +296,10 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles>::kThreads, Cfg<kD, kTiles>::kM
                       mbar_wait(&ctl.v_empty[sv], ((j / C::kStagesV) & 1) ^ 1, abort_flag, status, kWatchV + 1));
       if (!ok) break;
       if (leader) {
-        mbar_arrive_expect_tx(&ctl.v_full[sv], C::kTileBytes);
+        mbar_arrive_expect_tx(&ctl.v_full[sv], C::kKVBytes);
         for (int cb = 0; cb < kD / 64; ++cb)
-          tma_load_4d(smem_addr(sV + sv * C::kTileBytes + cb * C::kBlockBytes), &map_v, &ctl.v_full[sv], cb * 64,
-                      j * 128, hh, bb, pol_keep);
+          tma_load_4d(smem_addr(sV + sv * C::kKVBytes + cb * C::kKVBlockBytes), &map_v, &ctl.v_full[sv], cb * 64,
+                      j * C::kBN, hh, bb, pol_keep);
       }
       last_v[sv] = j;
       RA_MARK(6144 + j * 4 + 2);
@@ -311,10 +316,10 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles>::kThreads, Cfg<kD, kTiles>::kM
     }
   } else if (warp == C::kMmaWarp) {
     // ------------------------------------------------------------------ UMMA
-    const uint32_t idesc_s = umma_idesc_f16(kBf16, 128, 128, false);
+    const uint32_t idesc_s = umma_idesc_f16(kBf16, 128, C::kBN, false);
     const uint32_t idesc_o = umma_idesc_f16(kBf16, 128, kD, true);
     const bool leader = elect_one();
-    const uint32_t tS0 = tmem + 0, tS1 = tmem + 128;
+    const uint32_t tS0 = tmem + 0, tS1 = tmem + C::kBN;
     const uint32_t tO0 = tmem + C::kColO, tO1 = tmem + C::kColO + kD;
     const uint32_t q_addr0 = smem_addr(sQ), q_addr1 = smem_addr(sQ + C::kTileBytes);
 
@@ -322,8 +327,9 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles>::kThreads, Cfg<kD, kTiles>::kM
     auto issue_s = [&](uint32_t d_tmem, uint32_t q_addr, uint32_t k_addr) {
 #pragma unroll
       for (int k = 0; k < kD / 16; ++k) {
-        const uint32_t off = (k / 4) * C::kBlockBytes + (k % 4) * 32;
-        umma_ss(d_tmem, sw128_desc(q_addr + off, 16, 1024), sw128_desc(k_addr + off, 16, 1024), idesc_s,
+        const uint32_t q_off = (k / 4) * C::kBlockBytes + (k % 4) * 32;
+        const uint32_t k_off = (k / 4) * C::kKVBlockBytes + (k % 4) * 32;
+        umma_ss(d_tmem, sw128_desc(q_addr + q_off, 16, 1024), sw128_desc(k_addr + k_off, 16, 1024), idesc_s,
                 k > 0 ? 1u : 0u);
       }
     };
@@ -340,8 +346,8 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles>::kThreads, Cfg<kD, kTiles>::kM
         tc_fence_after();
         if (leader) {
 #pragma unroll
-          for (int k = 4 * h; k < 4 * h + 4; ++k)
-            umma_ts(d_tmem, p_tmem + k * 8, sw128_desc(v_addr + k * 2048, C::kBlockBytes, 1024), idesc_o,
+          for (int k = h * (C::kBN / 32); k < (h + 1) * (C::kBN / 32); ++k)
+            umma_ts(d_tmem, p_tmem + k * 8, sw128_desc(v_addr + k * 2048, C::kKVBlockBytes, 1024), idesc_o,
                     (acc || k > 0) ? 1u : 0u);
         }
         __syncwarp();
@@ -385,13 +391,13 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles>::kThreads, Cfg<kD, kTiles>::kM
             if (!ok) break;
             tc_fence_after();
             if (leader) {
-              issue_s(t == 0 ? tS0 : tS1, t == 0 ? q_addr0 : q_addr1, smem_addr(sK + sk1 * C::kTileBytes));
+              issue_s(t == 0 ? tS0 : tS1, t == 0 ? q_addr0 : q_addr1, smem_addr(sK + sk1 * C::kKVBytes));
               umma_commit(&ctl.s_full[t]);
             }
             __syncwarp();
           }
           if (j < nt[t]) {
-            ok = issue_pv(t, smem_addr(sV + sv * C::kTileBytes), j > 0, j & 1, kWatchP + 2 * t);
+            ok = issue_pv(t, smem_addr(sV + sv * C::kKVBytes), j > 0, j & 1, kWatchP + 2 * t);
             if (!ok) break;
             if (leader) {
               umma_commit(&ctl.p_free[t]);
@@ -412,7 +418,7 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles>::kThreads, Cfg<kD, kTiles>::kM
     // Issue order per key block j: S0(j), O1 += P1(j-1) V(j-1), S1(j), O0 += P0(j) V(j).
     for (int j = 0; j < nkb && ok; ++j) {
       const int sk = j % C::kStagesK, sv = j % C::kStagesV;
-      const uint32_t k_addr = smem_addr(sK + sk * C::kTileBytes);
+      const uint32_t k_addr = smem_addr(sK + sk * C::kKVBytes);
       RA_MARK(4096 + j * 8 + 0);
       ok = __all_sync(0xffffffffu,
                       mbar_wait(&ctl.k_full[sk], (j / C::kStagesK) & 1, abort_flag, status, kWatchK + 2));
@@ -426,7 +432,7 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles>::kThreads, Cfg<kD, kTiles>::kM
       RA_MARK(4096 + j * 8 + 1);
       if (j >= 1 && j - 1 < n1) {
         const int pv = (j - 1) % C::kStagesV;
-        ok = issue_pv(1, smem_addr(sV + pv * C::kTileBytes), j - 1 > 0, (j - 1) & 1, kWatchP + 2);
+        ok = issue_pv(1, smem_addr(sV + pv * C::kKVBytes), j - 1 > 0, (j - 1) & 1, kWatchP + 2);
         if (!ok) break;
         if (leader) umma_commit(&ctl.v_empty[pv]);
         __syncwarp();
@@ -450,7 +456,7 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles>::kThreads, Cfg<kD, kTiles>::kM
                       mbar_wait(&ctl.v_full[sv], (j / C::kStagesV) & 1, abort_flag, status, kWatchV + 2));
       if (!ok) break;
       if (j < n0) {
-        ok = issue_pv(0, smem_addr(sV + sv * C::kTileBytes), j > 0, j & 1, kWatchP + 0);
+        ok = issue_pv(0, smem_addr(sV + sv * C::kKVBytes), j > 0, j & 1, kWatchP + 0);
         if (!ok) break;
         if (leader && j == n0 - 1) umma_commit(&ctl.o_full[0]);
         __syncwarp();
@@ -461,7 +467,7 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles>::kThreads, Cfg<kD, kTiles>::kM
     }
     if (ok && n1 > 0 && n1 == nkb) {
       const int pv = (nkb - 1) % C::kStagesV;
-      ok = issue_pv(1, smem_addr(sV + pv * C::kTileBytes), nkb - 1 > 0, (nkb - 1) & 1, kWatchP + 4);
+      ok = issue_pv(1, smem_addr(sV + pv * C::kKVBytes), nkb - 1 > 0, (nkb - 1) & 1, kWatchP + 4);
       if (ok && leader) {
         umma_commit(&ctl.v_empty[pv]);
         umma_commit(&ctl.o_full[1]);
@@ -490,37 +496,54 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles>::kThreads, Cfg<kD, kTiles>::kM
     float l = 0.f;        // running sum of probabilities relative to m
     bool ok = true;
 
-    // Stores one 64-key half of P (P columns [32h, 32h+32)) and signals it.
+    constexpr int kBN = C::kBN;
+    // Stores half h of the block's P (keys [h*kBN/2, (h+1)*kBN/2), packed
+    // 16-bit pairs in P columns [h*kBN/4, (h+1)*kBN/4)) and signals it.
+    // With 128-key blocks pk holds the half; with 64-key blocks pk holds both
+    // halves, half h in pk[16h, 16h+16).
     auto store_half = [&](int h, const uint32_t (&pk)[32]) {
-      tmem_st32(tP + 32 * h, pk);
+      if constexpr (kBN == 128) {
+        tmem_st32(tP + 32 * h, pk);
+      } else {
+        uint32_t q[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) q[i] = pk[16 * h + i];
+        tmem_st16(tP + 16 * h, q);
+      }
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&ctl.p_full[t][h]);
     };
 
-    // Loads the 128 fp32 scores of this thread's row and masks keys past Lk
-    // and, when causal, keys after the query.
-    auto load_scores = [&](int j, float (&s)[128]) {
-      uint32_t u0[32], u1[32], u2[32], u3[32];
-      tmem_ld32(tS + 0, u0);
-      tmem_ld32(tS + 32, u1);
-      tmem_ld32(tS + 64, u2);
-      tmem_ld32(tS + 96, u3);
+    // Loads the block's kBN fp32 scores of this thread's row and masks keys
+    // past Lk and, when causal, keys after the query.
+    auto load_scores = [&](int j, float (&s)[kBN]) {
+      uint32_t u[kBN / 32][32];
+#pragma unroll
+      for (int cb = 0; cb < kBN / 32; ++cb) tmem_ld32(tS + 32 * cb, u[cb]);
       tmem_wait_ld();
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        s[i] = __uint_as_float(u0[i]);
-        s[32 + i] = __uint_as_float(u1[i]);
-        s[64 + i] = __uint_as_float(u2[i]);
-        s[96 + i] = __uint_as_float(u3[i]);
-      }
-      const int kbase = j * 128;
-      if ((kbase + 128 > p.Lk) || (kCausal && kbase + 127 > q0 + t * 128)) {
+      for (int cb = 0; cb < kBN / 32; ++cb)
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s[32 * cb + i] = __uint_as_float(u[cb][i]);
+      const int kbase = j * kBN;
+      if ((kbase + kBN > p.Lk) || (kCausal && kbase + kBN - 1 > q0 + t * 128)) {
         int limit = p.Lk - 1 - kbase;
         if (kCausal) limit = min(limit, row_abs - kbase);
 #pragma unroll
-        for (int i = 0; i < 128; ++i)
+        for (int i = 0; i < kBN; ++i)
           if (i > limit) s[i] = -INFINITY;
+      }
+    };
+    // Exponentials of the first half of the block's keys against the
+    // reference -nmc2/c2 (pk half 0 and its sums).
+    auto exp_half0 = [&](const float (&s)[kBN], uint64_t nmc2, uint32_t (&pk)[32], uint64_t& sum0,
+                         uint64_t& sum1) {
+      if constexpr (kBN == 128) {
+        exp_pack32<kBf16, 0, 0>(s, c2, nmc2, pk, sum0);
+        exp_pack32<kBf16, 32, 16>(s, c2, nmc2, pk, sum1);
+      } else {
+        exp_pack32<kBf16, 0, 0>(s, c2, nmc2, pk, sum0);
       }
     };
 
@@ -530,19 +553,20 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles>::kThreads, Cfg<kD, kTiles>::kM
       if (!ok) break;
       tc_fence_after();
       RA_MARK(t * 2048 + j * 16 + 1);
-      float s[128];
+      float s[kBN];
       load_scores(j, s);
       RA_MARK(t * 2048 + j * 16 + 2);
       // Row max of the block: four independent chains of 3-input max.
       float mx[4] = {s[0], s[1], s[2], s[3]};
 #pragma unroll
-      for (int i = 4; i < 124; i += 8) {
+      for (int i = 4; i < kBN - 4; i += 8) {
         mx[0] = fmax3(mx[0], s[i + 0], s[i + 4]);
         mx[1] = fmax3(mx[1], s[i + 1], s[i + 5]);
         mx[2] = fmax3(mx[2], s[i + 2], s[i + 6]);
         mx[3] = fmax3(mx[3], s[i + 3], s[i + 7]);
       }
-      const float mb = fmax3(fmax3(mx[0], mx[1], s[124]), fmax3(mx[2], mx[3], s[125]), fmaxf(s[126], s[127]));
+      const float mb = fmax3(fmax3(mx[0], mx[1], s[kBN - 4]), fmax3(mx[2], mx[3], s[kBN - 3]),
+                             fmaxf(s[kBN - 2], s[kBN - 1]));
 
       // Exponentials of the first half against the running max, computed
       // while the block max is still being reduced: after the first blocks
@@ -552,9 +576,7 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles>::kThreads, Cfg<kD, kTiles>::kM
       uint32_t pk[32];
       {
         const float mc = (m == -INFINITY) ? 0.f : m * c;
-        const uint64_t nmc2 = f2(-mc, -mc);
-        exp_pack32<kBf16, 0, 0>(s, c2, nmc2, pk, sum0);
-        exp_pack32<kBf16, 32, 16>(s, c2, nmc2, pk, sum1);
+        exp_half0(s, f2(-mc, -mc), pk, sum0, sum1);
       }
       RA_MARK(t * 2048 + j * 16 + 3);
       const bool grow = (fmaxf(m, mb) - m) * c > 8.0f;
@@ -589,11 +611,9 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles>::kThreads, Cfg<kD, kTiles>::kM
         }
         load_scores(j, s);
         const float mc = m * c;
-        const uint64_t nmc2 = f2(-mc, -mc);
         sum0 = f2(0.f, 0.f);
         sum1 = f2(0.f, 0.f);
-        exp_pack32<kBf16, 0, 0>(s, c2, nmc2, pk, sum0);
-        exp_pack32<kBf16, 32, 16>(s, c2, nmc2, pk, sum1);
+        exp_half0(s, f2(-mc, -mc), pk, sum0, sum1);
       }
       RA_MARK(t * 2048 + j * 16 + 4);
       if constexpr (C::kSepP) {
@@ -613,8 +633,12 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles>::kThreads, Cfg<kD, kTiles>::kM
       {
         const float mc = m * c;
         const uint64_t nmc2 = f2(-mc, -mc);
-        exp_pack32<kBf16, 64, 0>(s, c2, nmc2, pk, sum0);
-        exp_pack32<kBf16, 96, 16>(s, c2, nmc2, pk, sum1);
+        if constexpr (kBN == 128) {
+          exp_pack32<kBf16, 64, 0>(s, c2, nmc2, pk, sum0);
+          exp_pack32<kBf16, 96, 16>(s, c2, nmc2, pk, sum1);
+        } else {
+          exp_pack32<kBf16, 32, 16>(s, c2, nmc2, pk, sum1);
+        }
       }
       RA_MARK(t * 2048 + j * 16 + 6);
       store_half(1, pk);
@@ -690,16 +714,16 @@ struct Strides {
 // (the caller then runs the general kernel).
 constexpr int kNoTensorMap = -2;
 
-template <bool kBf16, int kD, bool kCausal, int kTiles>
+template <bool kBf16, int kD, bool kCausal, int kTiles, int kBlockKeys>
 static int launch_impl(const void* q, const void* k, const void* v, void* out, int B, int H, int Sq, int Skv,
                        const Strides& sq, const Strides& sk, const Strides& sv, float scale, cudaStream_t stream) {
-  using C = Cfg<kD, kTiles>;
+  using C = Cfg<kD, kTiles, kBlockKeys>;
   CUtensorMap mq, mk, mv, mo;
   const uint64_t D = kD;
   const int r[4] = {
       make_tensor_map_4d(&mq, q, kBf16, D, Sq, H, B, sq.l, sq.h, sq.b, 64, 128),
-      make_tensor_map_4d(&mk, k, kBf16, D, Skv, H, B, sk.l, sk.h, sk.b, 64, 128),
-      make_tensor_map_4d(&mv, v, kBf16, D, Skv, H, B, sv.l, sv.h, sv.b, 64, 128),
+      make_tensor_map_4d(&mk, k, kBf16, D, Skv, H, B, sk.l, sk.h, sk.b, 64, C::kBN),
+      make_tensor_map_4d(&mv, v, kBf16, D, Skv, H, B, sv.l, sv.h, sv.b, 64, C::kBN),
       make_tensor_map_4d(&mo, out, kBf16, D, Sq, H, B, D, static_cast<uint64_t>(Sq) * D,
                          static_cast<uint64_t>(H) * Sq * D, 64, 128)};
   for (int e : r)
@@ -707,7 +731,7 @@ static int launch_impl(const void* q, const void* k, const void* v, void* out, i
   for (int e : r)
     if (e != 0) return ATTN_ERR_TENSOR_MAP;
 
-  auto kern = attn_fwd_kernel<kBf16, kD, kCausal, kTiles>;
+  auto kern = attn_fwd_kernel<kBf16, kD, kCausal, kTiles, kBlockKeys>;
   // Opt in to the large dynamic shared-memory carve-out once per device.
   static bool configured[64] = {};
   static std::mutex mu;
@@ -744,15 +768,28 @@ static int launch_impl(const void* q, const void* k, const void* v, void* out, i
   return cudaGetLastError() == cudaSuccess ? ATTN_OK : ATTN_ERR_LAUNCH;
 }
 
-// Q tiles per CTA.  D=64: one, and two CTAs per SM (the TMEM of one tile is
-// 256 columns: S, P and O), so one CTA's set-up, first block and epilogue
-// overlap the other's softmax.  D=128: two, one CTA per SM (two one-tile
-// CTAs would have to single-buffer their 32 KB K and V blocks to fit).
-#ifndef RA_D64_TILES
-#define RA_D64_TILES 1
-#endif
-constexpr int kD64Tiles = RA_D64_TILES;
-constexpr int kD128Tiles = 2;
+// Multiprocessor count of the current device, cached per device (0 if it
+// cannot be read).
+static int sm_count() {
+  static int cached[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  if (cached[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
+
+// D=64 problems for 64-key blocks: with few blocks per unit the fixed cost of
+// a CTA (set-up, first block, epilogue) dominates, and three 64-key CTAs per
+// SM hide more of it than two 128-key ones, provided the grid fills the SMs
+// more than twice over; with many blocks per unit, or a small grid, the
+// 128-key CTAs are faster.
+static bool d64_short_keys(long long ctas, int Skv, bool causal) {
+  return ctas >= 2LL * sm_count() && Skv <= (causal ? 1024 : 384);
+}
 
 // Compute capability 10.x check, cached per device.
 static int check_device() {
@@ -835,18 +872,25 @@ extern "C" int launch_attn_forward_strided(const void* q, const void* k, const v
   if (dtype == ATTN_F32 || (D != 64 && D != 128) || !aligned(out, 16)) return general();
   const bool bf16 = dtype == ATTN_BF16;
   int st = ATTN_ERR_UNSUPPORTED;
-#define RA_DISPATCH(BF, DD, CA)                                                           \
-  if (bf16 == BF && D == DD && causal == CA)                                              \
-    st = launch_impl<BF, DD, CA, DD == 64 ? kD64Tiles : kD128Tiles>(q, k, v, out, B, H, Sq, Skv, sq, sk, sv, scale, stream); \
+  // D=128: two-tile CTAs.  D=64: one-tile CTAs with 128-key blocks (two per
+  // SM), or with 64-key blocks (three per SM) for short key ranges.
+  const int keys = (D == 64 && d64_short_keys(BH * ((Sq + 127) / 128), Skv, causal)) ? 64 : 128;
+#define RA_DISPATCH(BF, DD, CA, TILES, KEYS)                                                          \
+  if (bf16 == BF && D == DD && causal == CA && keys == KEYS)                                          \
+    st = launch_impl<BF, DD, CA, TILES, KEYS>(q, k, v, out, B, H, Sq, Skv, sq, sk, sv, scale, stream); \
   else
-  RA_DISPATCH(false, 128, false)
-  RA_DISPATCH(false, 128, true)
-  RA_DISPATCH(false, 64, false)
-  RA_DISPATCH(false, 64, true)
-  RA_DISPATCH(true, 128, false)
-  RA_DISPATCH(true, 128, true)
-  RA_DISPATCH(true, 64, false)
-  RA_DISPATCH(true, 64, true) {}
+  RA_DISPATCH(false, 128, false, 2, 128)
+  RA_DISPATCH(false, 128, true, 2, 128)
+  RA_DISPATCH(false, 64, false, 1, 128)
+  RA_DISPATCH(false, 64, true, 1, 128)
+  RA_DISPATCH(false, 64, false, 1, 64)
+  RA_DISPATCH(false, 64, true, 1, 64)
+  RA_DISPATCH(true, 128, false, 2, 128)
+  RA_DISPATCH(true, 128, true, 2, 128)
+  RA_DISPATCH(true, 64, false, 1, 128)
+  RA_DISPATCH(true, 64, true, 1, 128)
+  RA_DISPATCH(true, 64, false, 1, 64)
+  RA_DISPATCH(true, 64, true, 1, 64) {}
 #undef RA_DISPATCH
   return st == kNoTensorMap ? general() : st;
 }

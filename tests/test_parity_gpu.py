@@ -57,6 +57,20 @@ def test_cross_attention(attn, shape, dtype, causal):
     run_case(attn, shape, DT[dtype], causal)
 
 
+# D=64 problems the dispatcher sends to 64-key blocks (three CTAs per SM):
+# at least two CTAs per SM and short key ranges (<= 384 keys, <= 1024 causal),
+# with tails that are not multiples of 64 or 128.
+SHORT_KEYS = [Shape(16, 20, 160, 93, 64), Shape(8, 16, 384, 384, 64), Shape(8, 16, 512, 512, 64),
+              Shape(8, 40, 200, 300, 64), Shape(16, 5, 2560, 351, 64)]
+
+
+@pytest.mark.parametrize("dtype", ["fp16", "bf16"])
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("shape", SHORT_KEYS, ids=lambda s: f"{s.B}x{s.H}x{s.Lq}x{s.Lk}x{s.D}")
+def test_d64_short_key_blocks(attn, shape, dtype, causal):
+    run_case(attn, shape, DT[dtype], causal)
+
+
 @pytest.mark.parametrize("causal", [False, True])
 @pytest.mark.parametrize("D", [64, 128])
 def test_running_max_rescale(attn, D, causal):
