@@ -92,7 +92,7 @@ struct Cfg {
   static constexpr int kRows = kBM * kTiles;            // query rows per CTA
   // K / V ring depths.  One-tile CTAs run two (three with 64-key blocks) per
   // SM, so each keeps to its share of the SM's shared memory.
-  static constexpr int kStagesK = kBN == 64 ? 3 : (kD == 128 || kTiles == 1) ? 2 : 3;
+  static constexpr int kStagesK = (kBN == 64 || (kD == 64 && kTiles == 2)) ? 3 : 2;
   static constexpr int kStagesV = kStagesK;
   static constexpr uint32_t kTileBytes = 128u * kD * 2; // one 128 x D Q tile
   static constexpr uint32_t kBlockBytes = 128u * 128;   // one 64-column block of a Q tile
@@ -104,8 +104,8 @@ struct Cfg {
   // running.  Otherwise P aliases the first half of S.
   static constexpr bool kSepP = kD == 64 && kBN == 128;
   static constexpr uint32_t kTmemCols = kTiles == 2 ? 512 : (kBN == 64 ? 128 : 256);
-  static constexpr uint32_t kColP = 128 * kTiles;                        // P per tile (64 columns) when kSepP
-  static constexpr uint32_t kColO = kSepP ? 192 * kTiles : kBN * kTiles;  // O per tile (kD columns)
+  static constexpr uint32_t kColP = kBN * kTiles;                            // P per tile (64 columns) when kSepP
+  static constexpr uint32_t kColO = kSepP ? kColP + 64 * kTiles : kBN * kTiles;  // O per tile (kD columns)
   static constexpr int kMmaWarp = 4 * kTiles;            // after the softmax warpgroups
   static constexpr int kTmaWarp = 4 * kTiles + 1;
   static constexpr int kThreads = 128 * kTiles + 64;
@@ -487,7 +487,7 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles, kBlockKeys>::kThreads, Cfg<kD,
     const int row_abs = q0 + t * 128 + row_in_tile;
     const int n_t = t == 0 ? n0 : n1;
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    const uint32_t tS = tmem + lane_off + t * 128;
+    const uint32_t tS = tmem + lane_off + t * C::kBN;
     const uint32_t tP = C::kSepP ? tmem + lane_off + C::kColP + t * 64 : tS;
     const uint32_t tO = tmem + lane_off + C::kColO + t * kD;
     const float c = p.scale_log2;
