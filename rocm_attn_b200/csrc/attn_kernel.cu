@@ -571,7 +571,9 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles, kBlockKeys>::kThreads, Cfg<kD,
       // Exponentials of the first half against the running max, computed
       // while the block max is still being reduced: after the first blocks
       // the max almost never moves by more than 2^8, and then these values
-      // are final.
+      // are final.  The first block takes its own max as the running max
+      // (l and O are still zero), so it needs no second pass.
+      if (j == 0) m = mb;
       uint64_t sum0 = f2(0.f, 0.f), sum1 = f2(0.f, 0.f);
       uint32_t pk[32];
       {
