@@ -662,20 +662,23 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles, kBlockKeys>::kThreads, Cfg<kD,
     if (store) {
       tc_fence_after();
       const float inv_l = 1.f / l;
-#pragma unroll 1
-      for (int cc = 0; cc < kD; cc += 32) {
-        uint32_t o[32];
-        tmem_ld32(tO + cc, o);
-        tmem_wait_ld();
-        const int cb = cc / 64;
-        const int chunk0 = (cc % 64) / 8;
+      // The whole O row at once (one wait for all loads; the scores are dead).
+      uint32_t o[kD / 32][32];
+#pragma unroll
+      for (int cq = 0; cq < kD / 32; ++cq) tmem_ld32(tO + 32 * cq, o[cq]);
+      tmem_wait_ld();
+#pragma unroll
+      for (int cq = 0; cq < kD / 32; ++cq) {
+        const int cb = cq / 2;
+        const int chunk0 = (cq % 2) * 4;
 #pragma unroll
         for (int q4 = 0; q4 < 4; ++q4) {
+          const uint32_t* w = &o[cq][8 * q4];
           uint4 v;
-          v.x = pack2<kBf16>(__uint_as_float(o[8 * q4 + 0]) * inv_l, __uint_as_float(o[8 * q4 + 1]) * inv_l);
-          v.y = pack2<kBf16>(__uint_as_float(o[8 * q4 + 2]) * inv_l, __uint_as_float(o[8 * q4 + 3]) * inv_l);
-          v.z = pack2<kBf16>(__uint_as_float(o[8 * q4 + 4]) * inv_l, __uint_as_float(o[8 * q4 + 5]) * inv_l);
-          v.w = pack2<kBf16>(__uint_as_float(o[8 * q4 + 6]) * inv_l, __uint_as_float(o[8 * q4 + 7]) * inv_l);
+          v.x = pack2<kBf16>(__uint_as_float(w[0]) * inv_l, __uint_as_float(w[1]) * inv_l);
+          v.y = pack2<kBf16>(__uint_as_float(w[2]) * inv_l, __uint_as_float(w[3]) * inv_l);
+          v.z = pack2<kBf16>(__uint_as_float(w[4]) * inv_l, __uint_as_float(w[5]) * inv_l);
+          v.w = pack2<kBf16>(__uint_as_float(w[6]) * inv_l, __uint_as_float(w[7]) * inv_l);
           const int chunk = chunk0 + q4;
           const uint32_t off = cb * C::kBlockBytes + row_in_tile * 128 + ((chunk ^ (row_in_tile & 7)) << 4);
           *reinterpret_cast<uint4*>(stage + off) = v;
