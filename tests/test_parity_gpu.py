@@ -61,7 +61,8 @@ def test_cross_attention(attn, shape, dtype, causal):
 # at least two CTAs per SM and short key ranges (<= 384 keys, <= 1024 causal),
 # with tails that are not multiples of 64 or 128.
 SHORT_KEYS = [Shape(16, 20, 160, 93, 64), Shape(8, 16, 384, 384, 64), Shape(8, 16, 512, 512, 64),
-              Shape(8, 40, 200, 300, 64), Shape(16, 5, 2560, 351, 64)]
+              Shape(8, 40, 200, 300, 64), Shape(16, 5, 2560, 351, 64),
+              Shape(64, 8, 128, 1, 64), Shape(16, 20, 300, 100, 64)]  # one key; more queries than keys
 
 
 @pytest.mark.parametrize("dtype", ["fp16", "bf16"])
