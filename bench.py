@@ -9,6 +9,11 @@ metric quotes at 1/2/4/8 GPUs -- with the 64 (batch*head) slices sharded
 contiguously over the ranks (strong scaling: the total work is fixed, each
 rank runs the kernel on its own heads, no collective in the timed region).
 
+Inputs: i.i.d. N(0,1)*scale values drawn slice by slice, one CPU generator per
+(tensor, batch, head) seeded from --seed (``workloads.make_qkv``), so a rank
+draws exactly the heads it owns, the same values at every N, and the tests
+and the parity check below regenerate exactly these inputs.
+
 Timing: W untimed warm-up steps, then K steps, each bracketed by CUDA events
 on the launching stream; between timed steps a 256 MiB buffer is rewritten to
 flush L2 (outside the events); a barrier and a device synchronise on both
@@ -23,18 +28,28 @@ Reported on the line:
                 chunk on three streams
   roofline      tensor-bound: TFLOP/s of the kernel launches vs the measured
                 dense bf16 GEMM peak; traffic from the committed ncu summary
+  parity        max abs error of the timed step's output against the CPU
+                oracle (torch SDPA math, fp32) on a subset of heads and rows
+  per_config    N = 1: every other benchmark configuration (C1, C2, C3, the C5
+                sweep, the UnifoLM preset set) timed the same way, each with
+                its parity check and the same-box GPU comparators the
+                reference's benchmark offers (torch SDPA per backend, and
+                flash_attn_func when importable), run only for their times
   cpu_baseline  rank 0 at N=1: the reference path (torch SDPA as the
                 reference's _sdpa_fallback runs it) on the host cores, fp32,
                 on a bounded sample of the same workload's heads
-  clocks        nvidia-smi samples taken during the timed region
+  clocks        NVML samples taken during the timed region
   gather        N > 1 only: the NCCL all-gather that assembles the full O
                 on every rank, timed on its own after the timed region
 ``--impl reference`` times that CPU reference path alone on the same
-workload (rank 0; other ranks exit without work).
+workload (rank 0; other ranks exit without work).  It never imports the
+CUDA package: ``workloads.py`` is loaded by path.
 """
 from __future__ import annotations
 
 import argparse
+import dataclasses
+import importlib.util
 import json
 import os
 import statistics
@@ -48,14 +63,32 @@ REPO = os.path.dirname(os.path.abspath(__file__))
 if REPO not in sys.path:
     sys.path.insert(0, REPO)
 
-from rocm_attn_b200.workloads import (DTYPES, WORKLOADS, Shape, Workload, make_qkv, parse_shapes,  # noqa: E402
-                                      shard_range)
+
+def _load_workloads():
+    """``rocm_attn_b200/workloads.py`` (pure Python: shapes, seeded inputs,
+    sharding), loaded by path so that importing it does not run the package's
+    ``__init__``, which loads the CUDA extension.  The reference arm thus maps
+    none of this repository's native libraries."""
+    name = "rocm_attn_bench_workloads"
+    if name in sys.modules:
+        return sys.modules[name]
+    spec = importlib.util.spec_from_file_location(name, os.path.join(REPO, "rocm_attn_b200", "workloads.py"))
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+W = _load_workloads()
+DTYPES, WORKLOADS, Shape, Workload = W.DTYPES, W.WORKLOADS, W.Shape, W.Workload
 
 METRIC = "attention fwd ms/iter and TFLOPS (% of B200 fp16 TC peak) at 1/2/4/8 GPUs"
 SPEC_DENSE_FP16_TFLOPS = 2250.0
 FALLBACK_HBM_GBS = 6650.0  # earlier measurement on this pool, used without MEASURED_PEAKS.json
 FALLBACK_PEAK_TFLOPS = 1590.0
 L2_FLUSH_BYTES = 256 << 20
+L2_NOTE = "a 256 MiB buffer rewritten between timed steps, outside the timed region"
+PER_CONFIG = ("c1", "c2", "c3", "c4", "c5", "unifolm")
 
 
 def parse_args(argv=None):
@@ -74,6 +107,8 @@ def parse_args(argv=None):
     ap.add_argument("--cpu-sample-seconds", type=float, default=12.0)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-per-config", action="store_true", help="skip the per-configuration table (N=1)")
+    ap.add_argument("--no-parity", action="store_true", help="skip the oracle check of the timed inputs")
     ap.add_argument("--graph", action="store_true",
                     help="capture one step (all shapes of the workload) in a CUDA graph and time its replays: "
                          "removes the per-launch host overhead of small-shape workloads")
@@ -116,6 +151,13 @@ def profiled_traffic(workload_key: str, rank_heads: int, total_heads: int):
     except OSError:
         pass
     return None
+
+
+def config_of(w, seed: int) -> dict:
+    """The workload as both arms report it (identical dicts)."""
+    return {"workload": w.name, "shapes": [dataclasses.asdict(s) for s in w.shapes], "causal": w.causal,
+            "input_dtype": w.dtype, "inputs": f"N(0,1)*{w.value_scale:g} per (tensor, batch, head) slice",
+            "seed": seed, "l2": L2_NOTE}
 
 
 class ClockSampler:
@@ -180,57 +222,102 @@ class ClockSampler:
 def local_shapes(workload, world: int, rank: int):
     """Per-shape (batch*head) range owned by this rank.  Each shape is viewed
     as [1, B*H, L, D]; the slices of a rank are contiguous."""
-    out = []
-    for s in workload.shapes:
-        r = shard_range(s.bh, world, rank)
-        out.append((s, r))
-    return out
+    return [(s, W.shard_range(s.bh, world, rank)) for s in workload.shapes]
 
 
 def make_local_inputs(workload, shards, seed, device):
+    """q, k, v [1, len(range), L, D] per shape for the rank's (batch*head)
+    slices, drawn slice by slice from the seeded CPU generators."""
     dtype = DTYPES[workload.dtype]
-    tensors = []
+    out = []
     for s, r in shards:
         if len(r) == 0:
-            tensors.append(None)
+            out.append(None)
             continue
-        g = torch.Generator(device=device)
-        g.manual_seed(seed * 7919 + r.start)
-        shp_q = (1, len(r), s.Lq, s.D)
-        shp_k = (1, len(r), s.Lk, s.D)
-        q = (torch.randn(shp_q, device=device, generator=g) * workload.value_scale).to(dtype)
-        k = (torch.randn(shp_k, device=device, generator=g) * workload.value_scale).to(dtype)
-        v = (torch.randn(shp_k, device=device, generator=g) * workload.value_scale).to(dtype)
-        tensors.append((q, k, v))
-    return tensors
+        out.append(W.make_qkv(s, dtype, seed=seed, value_scale=workload.value_scale, bh_range=r, device=device))
+    return out
+
+
+def check_rows(L: int) -> list:
+    """Query rows the parity check covers: the first and the last 128 (the
+    longest causal rows), or every row of a short sequence."""
+    if L <= 256:
+        return list(range(L))
+    return list(range(128)) + list(range(L - 128, L))
+
+
+def parity_of(workload, shards, inputs, outs, causal: bool):
+    """Max abs error of ``outs`` against the CPU oracle (torch SDPA math,
+    fp32) on the first and last local head of each shape, over
+    :func:`check_rows`.  The oracle is the checker here; nothing it computes
+    is timed or returned as output."""
+    import oracle
+
+    dtype = DTYPES[workload.dtype]
+    worst = 0.0
+    finite = True
+    checked = []
+    for (s, r), t, o in zip(shards, inputs, outs):
+        if t is None:
+            continue
+        q, k, v = t
+        heads = sorted({0, len(r) - 1})
+        rows = check_rows(s.Lq)
+        for h in heads:
+            ref = oracle.sdpa_rows_fp32(q[:, h:h + 1], k[:, h:h + 1], v[:, h:h + 1], rows, causal=causal)
+            got = o[:, h:h + 1, rows].float().cpu()
+            finite = finite and bool(torch.isfinite(got).all())
+            worst = max(worst, oracle.max_abs_err(got, ref))
+        checked.append(f"{len(heads)} heads x {len(rows)} rows of {s.B}x{s.H}x{s.Lq}x{s.Lk}x{s.D}")
+    tol = oracle.ATOL[dtype]
+    return {"max_abs_err": worst, "tolerance": tol, "finite": finite, "ok": finite and worst <= tol,
+            "oracle": "torch SDPA math fp32 on CPU", "checked": "; ".join(checked)}
+
+
+def time_steps(fn, steps: int, warmup: int, flush, stream):
+    """Per-step milliseconds of ``fn`` (CUDA events on ``stream``, L2 flushed
+    between steps outside the events)."""
+    for _ in range(max(3, warmup)):
+        fn()
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    for i in range(steps):
+        flush.fill_(float(i))
+        starts[i].record(stream)
+        fn()
+        ends[i].record(stream)
+    torch.cuda.synchronize()
+    return [s.elapsed_time(e) for s, e in zip(starts, ends)]
 
 
 # ---------------------------------------------------------------- reference arm
 
 def cpu_reference_sample(workload, seconds: float, seed: int):
-    """Times the reference's CPU path (oracle.reference_sdpa_path, fp32, all
-    host threads) on whole (batch*head) slices of the workload until about
+    """Times the reference's CPU path (oracle.reference_sdpa_path: the
+    reference's _sdpa_fallback restated, fp32, all host threads) on whole
+    (batch*head) slices of the workload's seeded inputs until about
     `seconds` have elapsed.  Returns (TFLOP/s, cores, sample description)."""
     import oracle  # CPU reference leg only
 
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
+    dtype = DTYPES[workload.dtype]
     flops = 0.0
     t_total = 0.0
     done = []
-    for s in workload.shapes:
+    for i, s in enumerate(workload.shapes):
         per_head = s.flops(workload.causal) / s.bh
         n = 0
         for f in range(s.bh):
-            q, k, v = make_qkv(Shape(1, 1, s.Lq, s.Lk, s.D), torch.float32, seed=seed * 131 + f,
-                               value_scale=workload.value_scale)
-            q, k, v = (t.to(DTYPES[workload.dtype]).float() for t in (q, k, v))
+            q, k, v = W.make_qkv(s, dtype, seed=seed, value_scale=workload.value_scale, bh_range=[f])
+            q, k, v = (t.float() for t in (q, k, v))
             t0 = time.perf_counter()
             oracle.reference_sdpa_path(q, k, v, causal=workload.causal)
             t_total += time.perf_counter() - t0
             flops += per_head
             n += 1
-            if t_total >= seconds * (workload.shapes.index(s) + 1) / len(workload.shapes):
+            if t_total >= seconds * (i + 1) / len(workload.shapes):
                 break
         done.append(f"{n}/{s.bh} heads of {s.B}x{s.H}x{s.Lq}x{s.Lk}x{s.D}")
     return flops / t_total / 1e12, cores, "; ".join(done) + f" in {t_total:.1f}s (torch SDPA fp32, CPU)"
@@ -244,8 +331,10 @@ def run_reference_arm(args, rank, world):
     sample = None
     cores = os.cpu_count() or 1
     budget = max(2.0, min(30.0, 120.0 / max(1, args.steps + args.warmup)))
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32)
     for i in range(args.warmup + args.steps):
-        tf, cores, sample = cpu_reference_sample(w, budget, args.seed + i)
+        flush.fill_(float(i))  # the host caches start cold at every step, as the GPU arm's L2 does
+        tf, cores, sample = cpu_reference_sample(w, budget, args.seed)
         if i >= args.warmup:
             per_step.append(tf)
     value = statistics.median(per_step)
@@ -254,10 +343,14 @@ def run_reference_arm(args, rank, world):
         "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "TFLOP/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
-        "config": {"workload": w.name, "shapes": [s.__dict__ for s in w.shapes], "causal": w.causal,
-                   "sample": "bounded per step; ms_per_step extrapolated to the whole workload"},
+        "config": config_of(w, args.seed),
+        "method": "bounded sample of whole heads per step on the host cores; ms_per_step extrapolated to the "
+                  "whole workload",
         "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s", "cores": cores, "kind": "port",
-                         "sample": sample},
+                         "sample": sample,
+                         "what": "the reference's _sdpa_fallback (python/rocm_attn_op/__init__.py:7-26) restated "
+                                 "for CPU tensors (oracle.reference_sdpa_path); the reference's own Python package "
+                                 "cannot be installed without its HIP extension"},
         "e2e": {"value": round(value, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     return line
@@ -295,7 +388,108 @@ def time_gather(w, shards, step, world, rank, dev, stream, reps: int = 5):
     algbw = full_bytes / (ms * 1e-3) / 1e9
     return {"collective": "NCCL all_gather_into_tensor of O (sharding.gather_heads)", "ms": round(ms, 4),
             "bytes_gathered": int(full_bytes), "algbw_gbs": round(algbw, 1),
-            "busbw_gbs": round(algbw * (world - 1) / world, 1), "reps": reps}
+            "busbw_gbs": round(algbw * (world - 1) / world, 1), "reps": reps,
+            "nccl_version": ".".join(str(x) for x in torch.cuda.nccl.version())}
+
+
+def comparator_fns(w, inputs):
+    """Same-box GPU comparators on the same inputs, as the reference's
+    benchmark offers them (benchmark/bench_attention.py:103-145): torch SDPA
+    restricted to each backend -- FLASH first is what the reference's wrapper
+    runs on a CUDA device (python/rocm_attn_op/__init__.py:7-26) -- SDPA with
+    its default choice, and flash_attn_func when the package imports.  They
+    are timed only."""
+    import torch.nn.functional as F
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+
+    def sdpa(backend):
+        def fn():
+            for t in inputs:
+                if backend is None:
+                    F.scaled_dot_product_attention(t[0], t[1], t[2], is_causal=w.causal)
+                else:
+                    with sdpa_kernel(backend):
+                        F.scaled_dot_product_attention(t[0], t[1], t[2], is_causal=w.causal)
+        return fn
+
+    fns = {"sdpa_flash": sdpa(SDPBackend.FLASH_ATTENTION), "sdpa_efficient": sdpa(SDPBackend.EFFICIENT_ATTENTION),
+           "sdpa_cudnn": sdpa(SDPBackend.CUDNN_ATTENTION), "sdpa_default": sdpa(None)}
+    try:
+        from flash_attn import flash_attn_func
+        blhd = [tuple(x.transpose(1, 2).contiguous() for x in t) for t in inputs]
+
+        def fa():
+            for q, k, v in blhd:
+                flash_attn_func(q, k, v, causal=w.causal)
+        fns["flash_attn_func"] = fa
+    except Exception:
+        pass
+    return fns
+
+
+def per_config_table(args, dev, stream, flush, headline: dict):
+    """Every benchmark configuration on this GPU (N = 1): ours timed like the
+    headline, the parity check of its output, and the comparators."""
+    import rocm_attn_op
+
+    burst, _, peak_kind = measured_peaks()
+    hbm, _ = measured_hbm_gbs()
+    table = {}
+    for key in PER_CONFIG:
+        w = WORKLOADS[key]
+        row = {"workload": w.name}
+        try:
+            shards = local_shapes(w, 1, 0)
+            reuse = key == args.workload and headline
+            inputs = headline["inputs"] if reuse else make_local_inputs(w, shards, args.seed, dev)
+            steps = 20 if w.flops() > 2e11 else 50
+
+            def ours():
+                return [rocm_attn_op.attn_forward(t[0], t[1], t[2], causal=w.causal) for t in inputs]
+
+            if reuse:  # the headline's own timing
+                ms = headline["ms"]
+            else:
+                ms = statistics.median(time_steps(ours, steps, args.warmup, flush, stream))
+            tf = w.flops() / (ms * 1e-3) / 1e12
+            byts = sum(s.io_bytes() for s in w.shapes)
+            row.update({"ms": round(ms, 4), "tflops": round(tf, 2), "frac_of_measured_peak": round(tf / burst, 4),
+                        "frac_of_spec_2250": round(tf / SPEC_DENSE_FP16_TFLOPS, 4),
+                        "hbm_gbs": round(byts / (ms * 1e-3) / 1e9, 1),
+                        "frac_of_measured_hbm": round(byts / (ms * 1e-3) / 1e9 / hbm, 4)})
+            if len(w.shapes) > 1:
+                graph = torch.cuda.CUDAGraph()
+                ours()
+                torch.cuda.synchronize()
+                with torch.cuda.graph(graph):
+                    ours()
+                gms = statistics.median(time_steps(graph.replay, steps, args.warmup, flush, stream))
+                row["graph_ms"] = round(gms, 4)
+                del graph
+            if reuse and headline.get("parity") is not None:
+                row["parity"] = headline["parity"]
+            elif not args.no_parity:
+                outs = ours()
+                torch.cuda.synchronize()
+                row["parity"] = parity_of(w, shards, inputs, outs, w.causal)
+                del outs
+            comps = {}
+            for name, fn in comparator_fns(w, inputs).items():
+                try:
+                    cms = statistics.median(time_steps(fn, steps, args.warmup, flush, stream))
+                    comps[name] = {"ms": round(cms, 4), "tflops": round(w.flops() / (cms * 1e-3) / 1e12, 2),
+                                   "ours_speedup": round(cms / ms, 3)}
+                except Exception as e:  # backend not available for this shape or device
+                    comps[name] = {"error": str(e).splitlines()[0][:160]}
+                torch.cuda.synchronize()
+            row["comparators"] = comps
+            del inputs
+        except Exception as e:
+            row["error"] = repr(e)[:300]
+        table[key] = row
+        torch.cuda.empty_cache()
+    return {"peak_kind": f"{peak_kind} bf16 dense GEMM (burst) {burst} TFLOP/s; HBM {hbm} GB/s",
+            "timing": f"median of 20 steps (50 for workloads under 0.2 TFLOP), {L2_NOTE}", "rows": table}
 
 
 def run_ours(args, rank, world, local_rank):
@@ -322,6 +516,7 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize(dev)
     assert rocm_attn_op.check_status(local_rank) == 0, "kernel watchdog fired during warm-up"
     run = step
+    graph = None
     if args.graph:
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
@@ -348,12 +543,27 @@ def run_ours(args, rank, world, local_rank):
     step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
     total_ms = sum(step_ms)
     t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
+    rank_ms = None
     if dist:
+        every = torch.zeros(world, dtype=torch.float64, device=dev)
+        dist.all_gather_into_tensor(every, t)
+        rank_ms = [round(float(x) / args.steps, 4) for x in every.cpu()]
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     max_total_ms = float(t.item())
     ms_per_step = max_total_ms / args.steps
     tflops = w.flops() / (ms_per_step * 1e-3) / 1e12
     assert rocm_attn_op.check_status(local_rank) == 0, "kernel watchdog fired during timing"
+    if graph is not None:
+        del graph
+
+    # ---- parity of the timed inputs (oracle as checker, outside the timed region)
+    parity = None
+    if not args.no_parity:
+        outs = iter(step())
+        local_outs = [next(outs) if t is not None else None for t in inputs]
+        torch.cuda.synchronize(dev)
+        parity = parity_of(w, shards, inputs, local_outs, w.causal)
+        del local_outs, outs
 
     # ---- roofline of the kernel on this rank (one launch per shape per step)
     local_flops = sum(s.flops(w.causal) * len(r) / s.bh for s, r in shards)
@@ -380,6 +590,14 @@ def run_ours(args, rank, world, local_rank):
     # ---- the all-gather that assembles the full O on every rank (N > 1 only;
     # outside the timed region, reported on its own)
     gather = time_gather(w, shards, step, world, rank, dev, stream) if dist else None
+
+    # ---- every benchmark configuration with same-box comparators (N = 1)
+    per_config = None
+    if world == 1 and not args.no_per_config:
+        with ClockSampler(dev.index) as clk_table:
+            per_config = per_config_table(args, dev, stream, flush,
+                                          {"ms": ms_per_step, "inputs": inputs, "parity": parity})
+        per_config["clocks"] = clk_table.summary()
 
     # ---- end to end through the public API with pinned host buffers
     e2e = None
@@ -432,16 +650,18 @@ def run_ours(args, rank, world, local_rank):
         "metric": METRIC, "value": round(tflops, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": w.dtype, "data": "synthetic",
-        "config": {"workload": w.name, "shapes": [s.__dict__ for s in w.shapes], "causal": w.causal,
-                   "sharding": "contiguous (batch*head) slices per rank, no collective in the timed region",
-                   "l2": "256 MiB buffer rewritten between timed steps (outside the events)",
-                   "cuda_graph": bool(args.graph),
-                   "frac_of_spec_dense_fp16": round(tflops / world / SPEC_DENSE_FP16_TFLOPS, 4)},
+        "config": config_of(w, args.seed),
+        "sharding": "contiguous (batch*head) slices per rank, no collective in the timed region",
+        "cuda_graph": bool(args.graph),
+        "frac_of_spec_dense_fp16": round(tflops / world / SPEC_DENSE_FP16_TFLOPS, 4),
+        "rank_ms_per_step": rank_ms,
+        "parity": parity,
         "e2e": e2e,
         "gather": gather,
         "gpu_launches": args.steps * sum(1 for _, r in shards if len(r) > 0),
         "roofline": roofline,
         "clocks": clocks,
+        "per_config": per_config,
     }
     return line
 
@@ -450,7 +670,8 @@ def main(argv=None):
     args = parse_args(argv)
     if args.shapes:
         WORKLOADS["custom"] = Workload("custom-" + args.shapes.replace(";", "_") + ("-causal" if args.causal else "")
-                                       + "-" + args.dtype, tuple(parse_shapes(args.shapes)), args.dtype, args.causal)
+                                       + "-" + args.dtype, tuple(W.parse_shapes(args.shapes)), args.dtype,
+                                       args.causal)
         args.workload = "custom"
     elif args.workload == "custom":
         raise SystemExit("--workload custom needs --shapes")

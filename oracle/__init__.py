@@ -44,10 +44,20 @@ REF_KAT_BIN = os.path.join(HERE, "_ref", "attn_test_kat")
 ATOL = {torch.float16: 2e-3, torch.bfloat16: 1e-2, torch.float32: 1e-3}
 
 
-def build(reference_dir: str = "/root/reference") -> None:
-    """Compile the C oracle and, when the reference sources are present, the
-    reference's known-answer test against it (outputs stay in oracle/)."""
-    subprocess.run(["make", "-s", "-C", HERE, f"REF={reference_dir}"], check=True)
+def reference_dir() -> Optional[str]:
+    """Checkout of the reference's sources, if one is present: the directory
+    named by the ROCM_ATTN_REF environment variable, else a ``reference``
+    directory beside this repository.  None when neither exists."""
+    cand = os.environ.get("ROCM_ATTN_REF") or os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
+    return cand if os.path.isfile(os.path.join(cand, "src", "tests", "attn_test.cpp")) else None
+
+
+def build(ref_dir: Optional[str] = None) -> None:
+    """Compile the C oracle and, when the reference sources are present
+    (``ref_dir``, else :func:`reference_dir`), the reference's known-answer
+    test against it (outputs stay in oracle/)."""
+    ref = ref_dir or reference_dir() or ""
+    subprocess.run(["make", "-s", "-C", HERE, f"REF={ref}"], check=True)
 
 
 _lib = None
@@ -113,6 +123,27 @@ def sdpa_math_fp32(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bo
                                               scale=scale)
 
 
+def sdpa_rows_fp32(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, rows, causal: bool = False,
+                   scale: Optional[float] = None) -> torch.Tensor:
+    """:func:`sdpa_math_fp32` for the query rows ``rows`` (absolute row
+    indices, the same for every (b, h)) only: the causal rule keeps key j for
+    query row i when j <= i, as for the full problem.  Returns an fp32 CPU
+    tensor [B, H, len(rows), D]."""
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+
+    idx = torch.as_tensor(list(rows), dtype=torch.long)
+    qf = q.detach().to("cpu", torch.float32)[:, :, idx]
+    kf = k.detach().to("cpu", torch.float32)
+    vf = v.detach().to("cpu", torch.float32)
+    if kf.shape[2] == 0:
+        return torch.zeros_like(qf)
+    mask = None
+    if causal:
+        mask = torch.arange(kf.shape[2])[None, :] <= idx[:, None]
+    with sdpa_kernel(SDPBackend.MATH):
+        return F.scaled_dot_product_attention(qf, kf, vf, attn_mask=mask, dropout_p=0.0, scale=scale)
+
+
 def reference_sdpa_path(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = False) -> torch.Tensor:
     """The reference's ``_sdpa_fallback`` (python/rocm_attn_op/__init__.py:7-26)
     restated for CPU tensors: FLASH backend, else EFFICIENT, else default."""
@@ -171,5 +202,5 @@ def run_reference_kat() -> tuple[bool, str]:
     return r.returncode == 0 and "PASSED" in r.stdout, r.stdout.strip()
 
 
-__all__ = ["ATOL", "HALF_ULP", "build", "c_oracle_forward", "sdpa_math_fp32", "reference_sdpa_path", "max_abs_err", "check",
+__all__ = ["ATOL", "HALF_ULP", "build", "reference_dir", "c_oracle_forward", "sdpa_math_fp32", "sdpa_rows_fp32", "reference_sdpa_path", "max_abs_err", "check",
            "run_reference_kat"]

@@ -36,12 +36,50 @@
 
 #include "attn_general.h"
 
+#include <atomic>
+#include <mutex>
+
 namespace ra {
 
 namespace {
 
 constexpr int kRows = 64;    // query rows per CTA
 constexpr int kThreads = 256;
+constexpr int kMaxDevices = 64;
+
+// Multiprocessor count of the current device, read once per device (0 when
+// it cannot be read).
+int current_sm_count() {
+  static std::atomic<int> cached[kMaxDevices];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 0;
+  int n = cached[dev].load(std::memory_order_relaxed);
+  if (n == 0) {
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+    cached[dev].store(n, std::memory_order_relaxed);
+  }
+  return n;
+}
+
+// Raises the dynamic shared-memory limit of one kernel to `smem` bytes on the
+// current device, once per device; one static instance per kernel.
+struct SmemOptIn {
+  std::atomic<bool> done[kMaxDevices] = {};
+  std::mutex mu;
+  template <typename Kernel>
+  bool ensure(Kernel kern, int smem) {
+    if (smem <= 48 * 1024) return true;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return false;
+    if (done[dev].load(std::memory_order_acquire)) return true;
+    std::lock_guard<std::mutex> g(mu);
+    if (!done[dev].load(std::memory_order_relaxed)) {
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return false;
+      done[dev].store(true, std::memory_order_release);
+    }
+    return true;
+  }
+};
 
 template <typename T> __device__ __forceinline__ float to_f32(T x);
 template <> __device__ __forceinline__ float to_f32<float>(float x) { return x; }
@@ -214,6 +252,19 @@ __device__ __forceinline__ void load_f32x8(const void* src, int dtype, float* ds
 // holds 32 dims, 16 at D = 16): the warp covers 32 / lanes rows.
 __host__ __device__ constexpr int small_lanes_per_row(int D) { return D <= 32 ? 1 : D / 32; }
 
+// Largest dynamic shared memory a CTA may opt in to on sm_100 (227 KiB).
+constexpr int kMaxDynamicSmem = 232448;
+
+// Key capacity of the SIMT short-sequence kernel for Skv keys (16 or 64).
+__host__ __device__ constexpr int small_simt_keys(int Skv) { return Skv <= 16 ? 16 : 64; }
+
+// Dynamic shared memory of the SIMT short-sequence kernel: every warp holds
+// its slice's K and V as fp32.  At D = 128 with 64 keys this is 256 KiB, above
+// the limit, so those problems run the general kernel.
+__host__ __device__ constexpr int small_simt_smem_bytes(int D, int keys) {
+  return kSmallWarps * 2 * keys * D * static_cast<int>(sizeof(float));
+}
+
 // kD: the head dim (16, 32, 64 or 128); kKeys: the key capacity (16 or 64).
 // dtype and causal are the same for the whole launch.
 template <int kD, int kKeys>
@@ -343,15 +394,12 @@ __global__ void __launch_bounds__(kSmallWarps * 32) attn_small_kernel(const void
 template <int kD, int kKeys>
 int launch_small_typed(const void* q, const void* k, const void* v, void* out, int dtype, bool causal, int BH, int H,
                        int Sq, int Skv, float scale_log2, const GeneralStrides& st, cudaStream_t stream) {
-  const int smem = kSmallWarps * 2 * kKeys * kD * static_cast<int>(sizeof(float));
+  constexpr int smem = small_simt_smem_bytes(kD, kKeys);
+  static_assert(smem <= kMaxDynamicSmem, "SIMT short-sequence kernel above the shared-memory limit");
   auto kern = attn_small_kernel<kD, kKeys>;
-  int dev = 0, sms = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess ||
-      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-    return -1;
-  if (smem > 48 * 1024 &&
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-    return -1;
+  static SmemOptIn opt_in;
+  const int sms = current_sm_count();
+  if (sms == 0 || !opt_in.ensure(kern, smem)) return -1;
   const long long need = (static_cast<long long>(BH) + kSmallWarps - 1) / kSmallWarps;
   const unsigned grid = static_cast<unsigned>(need < 32LL * sms ? need : 32LL * sms);
   kern<<<grid, kSmallWarps * 32, smem, stream>>>(q, k, v, out, dtype, causal, BH, H, Sq, Skv, scale_log2, st);
@@ -363,7 +411,9 @@ int launch_small_keys(const void* q, const void* k, const void* v, void* out, in
                       int Sq, int Skv, float scale_log2, const GeneralStrides& st, cudaStream_t stream) {
   if (Skv <= 16)
     return launch_small_typed<kD, 16>(q, k, v, out, dtype, causal, BH, H, Sq, Skv, scale_log2, st, stream);
-  return launch_small_typed<kD, 64>(q, k, v, out, dtype, causal, BH, H, Sq, Skv, scale_log2, st, stream);
+  if constexpr (small_simt_smem_bytes(kD, 64) <= kMaxDynamicSmem)
+    return launch_small_typed<kD, 64>(q, k, v, out, dtype, causal, BH, H, Sq, Skv, scale_log2, st, stream);
+  return -2;  // does not fit in shared memory: the caller runs the general kernel
 }
 
 // ---------------------------------------------------------------------------
@@ -568,15 +618,12 @@ __global__ void __launch_bounds__(kMmaWarps * 32) attn_small_mma_kernel(const ui
 template <bool kBf16, int kD, int kNK>
 int launch_small_mma_typed(const void* q, const void* k, const void* v, void* out, bool causal, int BH, int H, int Sq,
                            int Skv, float scale_log2, const GeneralStrides& st, cudaStream_t stream) {
-  const int smem = kMmaWarps * (16 + 2 * 16 * kNK) * (kD + 8) * 2;
+  constexpr int smem = kMmaWarps * (16 + 2 * 16 * kNK) * (kD + 8) * 2;
+  static_assert(smem <= kMaxDynamicSmem, "short-sequence tensor-core kernel above the shared-memory limit");
   auto kern = attn_small_mma_kernel<kBf16, kD, kNK>;
-  int dev = 0, sms = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess ||
-      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-    return -1;
-  if (smem > 48 * 1024 &&
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-    return -1;
+  static SmemOptIn opt_in;
+  const int sms = current_sm_count();
+  if (sms == 0 || !opt_in.ensure(kern, smem)) return -1;
   const long long need = (static_cast<long long>(BH) + kMmaWarps - 1) / kMmaWarps;
   const unsigned grid = static_cast<unsigned>(need < 32LL * sms ? need : 32LL * sms);
   kern<<<grid, kMmaWarps * 32, smem, stream>>>(static_cast<const uint16_t*>(q), static_cast<const uint16_t*>(k),
@@ -778,11 +825,11 @@ __global__ void __launch_bounds__(kMidWarps * 32) attn_mid_mma_kernel(const uint
 template <bool kBf16, int kD>
 int launch_mid_typed(const void* q, const void* k, const void* v, void* out, bool causal, int BH, int H, int Sq,
                      int Skv, float scale_log2, const GeneralStrides& st, cudaStream_t stream) {
-  const int smem = 5 * 64 * (kD + 8) * 2;  // Q + two buffers of K and V
+  constexpr int smem = 5 * 64 * (kD + 8) * 2;  // Q + two buffers of K and V
+  static_assert(smem <= kMaxDynamicSmem, "mid-length kernel above the shared-memory limit");
   auto kern = attn_mid_mma_kernel<kBf16, kD>;
-  if (smem > 48 * 1024 &&
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-    return -1;
+  static SmemOptIn opt_in;
+  if (!opt_in.ensure(kern, smem)) return -1;
   const long long grid = static_cast<long long>(BH) * ((Sq + 63) / 64);
   if (grid > 0x7fffffffLL) return -1;
   kern<<<static_cast<unsigned>(grid), kMidWarps * 32, smem, stream>>>(
@@ -833,7 +880,9 @@ bool small_kernel_takes(int Sq, int Skv, int D, int dtype) {
   if (D != 16 && D != 32 && D != 64 && D != 128) return false;
   if (Sq < 1 || Skv < 1 || Skv > kSmallMaxKeys) return false;
   if (dtype != 2 && Sq <= 16) return true;  // warp-level tensor-core kernel: one m16 tile
-  return Sq <= 32 / small_lanes_per_row(D);  // SIMT kernel: one lane group per row
+  // SIMT kernel: one lane group per row, and the slice's K and V as fp32 in
+  // shared memory.
+  return Sq <= 32 / small_lanes_per_row(D) && small_simt_smem_bytes(D, small_simt_keys(Skv)) <= kMaxDynamicSmem;
 }
 
 int launch_attn_small(const void* q, const void* k, const void* v, void* out, int B, int H, int Sq, int Skv, int D,

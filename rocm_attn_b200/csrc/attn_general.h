@@ -27,7 +27,8 @@ int launch_attn_general(const void* q, const void* k, const void* v, void* out, 
 // Bounds of the short-sequence kernels (one warp per (batch, head) slice): D
 // in {16, 32, 64, 128}, Skv <= kSmallMaxKeys, and Sq <= 16 for fp16/bf16
 // (warp-level tensor cores) or, for the SIMT kernel, Sq <= 32 rows at D <= 32,
-// 16 at D = 64, 8 at D = 128.
+// 16 at D = 64, 8 at D = 128 (and at D = 128 only Skv <= 16: with more keys
+// its fp32 K and V do not fit in shared memory).
 constexpr int kSmallMaxKeys = 64;
 
 // True when launch_attn_small takes a problem of these sizes.

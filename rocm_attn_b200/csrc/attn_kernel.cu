@@ -44,6 +44,8 @@
 #include "attn_general.h"
 
 #include <math.h>
+
+#include <atomic>
 #include <mutex>
 
 namespace ra {
@@ -81,6 +83,7 @@ struct AttnParams {
   int num_qblocks;  // ceil(Lq / query rows per CTA)
   int head_group;   // causal: heads per scheduling group (their K/V fit in L2)
   float scale_log2; // softmax scale * log2(e)
+  unsigned long long wait_ns;  // limit of every pipeline wait (the watchdog)
 };
 
 // Compile-time shape of the pipeline for head dimension kD, kTiles 128-row
@@ -186,6 +189,7 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles, kBlockKeys>::kThreads, Cfg<kD,
   uint8_t* sV = sK + C::kStagesK * C::kKVBytes;         // kStagesV blocks
   volatile int* abort_flag = &ctl.abort_flag;
   int* status = &g_attn_status;
+  const uint64_t wait_ns = p.wait_ns;
 
   const int warp = __shfl_sync(0xffffffffu, static_cast<int>(threadIdx.x) / 32, 0);
   const int lane = threadIdx.x & 31;
@@ -284,7 +288,7 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles, kBlockKeys>::kThreads, Cfg<kD,
       const int sk = j % C::kStagesK;
       RA_MARK(6144 + j * 4 + 0);
       ok = __all_sync(0xffffffffu,
-                      mbar_wait(&ctl.k_empty[sk], ((j / C::kStagesK) & 1) ^ 1, abort_flag, status, kWatchK + 1));
+                      mbar_wait(&ctl.k_empty[sk], ((j / C::kStagesK) & 1) ^ 1, abort_flag, status, kWatchK + 1, wait_ns));
       if (!ok) break;
       if (leader) {
         mbar_arrive_expect_tx(&ctl.k_full[sk], C::kKVBytes);
@@ -296,7 +300,7 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles, kBlockKeys>::kThreads, Cfg<kD,
       RA_MARK(6144 + j * 4 + 1);
       const int sv = j % C::kStagesV;
       ok = __all_sync(0xffffffffu,
-                      mbar_wait(&ctl.v_empty[sv], ((j / C::kStagesV) & 1) ^ 1, abort_flag, status, kWatchV + 1));
+                      mbar_wait(&ctl.v_empty[sv], ((j / C::kStagesV) & 1) ^ 1, abort_flag, status, kWatchV + 1, wait_ns));
       if (!ok) break;
       if (leader) {
         mbar_arrive_expect_tx(&ctl.v_full[sv], C::kKVBytes);
@@ -344,7 +348,7 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles, kBlockKeys>::kThreads, Cfg<kD,
       const uint32_t p_tmem = C::kSepP ? tmem + C::kColP + t * 64 : (t == 0 ? tS0 : tS1);
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        if (!__all_sync(0xffffffffu, mbar_wait(&ctl.p_full[t][h], parity, abort_flag, status, code + h)))
+        if (!__all_sync(0xffffffffu, mbar_wait(&ctl.p_full[t][h], parity, abort_flag, status, code + h, wait_ns)))
           return false;
         tc_fence_after();
         if (leader) {
@@ -358,15 +362,15 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles, kBlockKeys>::kThreads, Cfg<kD,
       return true;
     };
 
-    bool ok = __all_sync(0xffffffffu, mbar_wait(&ctl.q_full[0], 0, abort_flag, status, kWatchQ + 2));
+    bool ok = __all_sync(0xffffffffu, mbar_wait(&ctl.q_full[0], 0, abort_flag, status, kWatchQ + 2, wait_ns));
     if constexpr (C::kSepP) {
       // Issue order: S0(0) S1(0) | per block j: S0(j+1) O0+=P0(j)V(j) S1(j+1) O1+=P1(j)V(j).
       // S(j+1) only waits for the softmax to have read S(j) (s_free), so the
       // scores of the next block are ready when the softmax finishes.
       const int nt[2] = {n0, n1};
-      if (ok && n1 > 0) ok = __all_sync(0xffffffffu, mbar_wait(&ctl.q_full[1], 0, abort_flag, status, kWatchQ + 3));
+      if (ok && n1 > 0) ok = __all_sync(0xffffffffu, mbar_wait(&ctl.q_full[1], 0, abort_flag, status, kWatchQ + 3, wait_ns));
       if (ok) {
-        ok = __all_sync(0xffffffffu, mbar_wait(&ctl.k_full[0], 0, abort_flag, status, kWatchK + 2));
+        ok = __all_sync(0xffffffffu, mbar_wait(&ctl.k_full[0], 0, abort_flag, status, kWatchK + 2, wait_ns));
         if (ok) {
           tc_fence_after();
           if (leader) {
@@ -386,11 +390,11 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles, kBlockKeys>::kThreads, Cfg<kD,
           if (!ok) break;
         }
         ok = __all_sync(0xffffffffu,
-                        mbar_wait(&ctl.v_full[sv], (j / C::kStagesV) & 1, abort_flag, status, kWatchV + 2));
+                        mbar_wait(&ctl.v_full[sv], (j / C::kStagesV) & 1, abort_flag, status, kWatchV + 2, wait_ns));
         if (!ok) break;
         for (int t = 0; t < 2 && ok; ++t) {
           if (j + 1 < nt[t]) {
-            ok = __all_sync(0xffffffffu, mbar_wait(&ctl.s_free[t], j & 1, abort_flag, status, kWatchS + 5 + t));
+            ok = __all_sync(0xffffffffu, mbar_wait(&ctl.s_free[t], j & 1, abort_flag, status, kWatchS + 5 + t, wait_ns));
             if (!ok) break;
             tc_fence_after();
             if (leader) {
@@ -424,7 +428,7 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles, kBlockKeys>::kThreads, Cfg<kD,
       const uint32_t k_addr = smem_addr(sK + sk * C::kKVBytes);
       RA_MARK(4096 + j * 8 + 0);
       ok = __all_sync(0xffffffffu,
-                      mbar_wait(&ctl.k_full[sk], (j / C::kStagesK) & 1, abort_flag, status, kWatchK + 2));
+                      mbar_wait(&ctl.k_full[sk], (j / C::kStagesK) & 1, abort_flag, status, kWatchK + 2, wait_ns));
       if (!ok) break;
       tc_fence_after();
       if (leader && j < n0) {
@@ -442,7 +446,7 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles, kBlockKeys>::kThreads, Cfg<kD,
       }
       RA_MARK(4096 + j * 8 + 2);
       if (j == 0 && n1 > 0) {
-        ok = __all_sync(0xffffffffu, mbar_wait(&ctl.q_full[1], 0, abort_flag, status, kWatchQ + 3));
+        ok = __all_sync(0xffffffffu, mbar_wait(&ctl.q_full[1], 0, abort_flag, status, kWatchQ + 3, wait_ns));
         if (!ok) break;
         tc_fence_after();
       }
@@ -456,7 +460,7 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles, kBlockKeys>::kThreads, Cfg<kD,
       __syncwarp();
       RA_MARK(4096 + j * 8 + 3);
       ok = __all_sync(0xffffffffu,
-                      mbar_wait(&ctl.v_full[sv], (j / C::kStagesV) & 1, abort_flag, status, kWatchV + 2));
+                      mbar_wait(&ctl.v_full[sv], (j / C::kStagesV) & 1, abort_flag, status, kWatchV + 2, wait_ns));
       if (!ok) break;
       if (j < n0) {
         ok = issue_pv(0, smem_addr(sV + sv * C::kKVBytes), j > 0, j & 1, kWatchP + 0);
@@ -552,7 +556,7 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles, kBlockKeys>::kThreads, Cfg<kD,
 
     for (int j = 0; j < n_t; ++j) {
       RA_MARK(t * 2048 + j * 16 + 0);
-      ok = __all_sync(0xffffffffu, mbar_wait(&ctl.s_full[t], j & 1, abort_flag, status, kWatchS + 1 + t));
+      ok = __all_sync(0xffffffffu, mbar_wait(&ctl.s_full[t], j & 1, abort_flag, status, kWatchS + 1 + t, wait_ns));
       if (!ok) break;
       tc_fence_after();
       RA_MARK(t * 2048 + j * 16 + 1);
@@ -599,7 +603,7 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles, kBlockKeys>::kThreads, Cfg<kD,
         if (C::kSepP && j > 0) {
           // Separate-P layout: S(j) may retire before the product of block
           // j-1, so wait for that product before touching O.
-          ok = __all_sync(0xffffffffu, mbar_wait(&ctl.p_free[t], (j - 1) & 1, abort_flag, status, kWatchO + 5 + t));
+          ok = __all_sync(0xffffffffu, mbar_wait(&ctl.p_free[t], (j - 1) & 1, abort_flag, status, kWatchO + 5 + t, wait_ns));
           if (!ok) break;
           tc_fence_after();
         }
@@ -628,7 +632,7 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles, kBlockKeys>::kThreads, Cfg<kD,
         tc_fence_before();
         mbar_arrive(&ctl.s_free[t]);
         if (j > 0) {
-          ok = __all_sync(0xffffffffu, mbar_wait(&ctl.p_free[t], (j - 1) & 1, abort_flag, status, kWatchO + 5 + t));
+          ok = __all_sync(0xffffffffu, mbar_wait(&ctl.p_free[t], (j - 1) & 1, abort_flag, status, kWatchO + 5 + t, wait_ns));
           if (!ok) break;
           tc_fence_after();
         }
@@ -659,7 +663,7 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles, kBlockKeys>::kThreads, Cfg<kD,
     // ------------------------------------------------------------- epilogue
     bool store = ok && n_t > 0;
     if (store) {
-      store = __all_sync(0xffffffffu, mbar_wait(&ctl.o_full[t], 0, abort_flag, status, kWatchO + 1 + t));
+      store = __all_sync(0xffffffffu, mbar_wait(&ctl.o_full[t], 0, abort_flag, status, kWatchO + 1 + t, wait_ns));
     }
     uint8_t* stage = sQ + t * C::kTileBytes;  // Q tile t is dead once O_t is final
     if (store) {
@@ -717,6 +721,10 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles, kBlockKeys>::kThreads, Cfg<kD,
 struct Strides {
   long long b, h, l;
 };
+
+// Pipeline wait limit for launches from now on (attn_set_wait_limit_ns);
+// 0 selects kWaitTimeoutNs.
+static std::atomic<unsigned long long> g_wait_limit_ns{0};
 
 // Returned by launch_impl when a buffer or stride cannot be described to TMA
 // (the caller then runs the general kernel).
@@ -777,6 +785,8 @@ static int launch_impl(const void* q, const void* k, const void* v, void* out, i
   const double kv_bytes = 2.0 * Skv * kD * 2;
   prm.head_group = static_cast<int>(fmax(1.0, fmin(static_cast<double>(BH), RA_HEAD_GROUP_BYTES / kv_bytes)));
   prm.scale_log2 = scale * 1.4426950408889634f;
+  const unsigned long long limit = g_wait_limit_ns.load(std::memory_order_relaxed);
+  prm.wait_ns = limit != 0 ? limit : kWaitTimeoutNs;
   const long long grid = static_cast<long long>(prm.num_qblocks) * BH;
   if (grid > 0x7fffffffLL) return ATTN_ERR_INVALID_ARGUMENT;
   kern<<<static_cast<unsigned>(grid), C::kThreads, C::kSmemBytes, stream>>>(mq, mk, mv, mo, prm);
@@ -870,17 +880,18 @@ extern "C" int launch_attn_forward_strided(const void* q, const void* k, const v
   };
   // Short sequences (a few dozen rows per head): one warp per (batch, head)
   // slice instead of a mostly empty 128- or 256-row tcgen05 unit.
-  if (small_kernel_takes(Sq, Skv, D, static_cast<int>(dtype))) {
-    const int r = launch_attn_small(q, k, v, out, B, H, Sq, Skv, D, causal, scale, static_cast<int>(dtype), gs, stream);
-    if (r != -2) return r == 0 ? ATTN_OK : ATTN_ERR_LAUNCH;  // -2: rows not 16-byte aligned, run the general kernel
-  }
+  // A short or mid-length launcher that returns non-zero launched nothing
+  // (-2: rows not 16-byte aligned; -1: it could not be configured), and the
+  // general kernel, which takes every problem, runs instead.
+  if (small_kernel_takes(Sq, Skv, D, static_cast<int>(dtype)) &&
+      launch_attn_small(q, k, v, out, B, H, Sq, Skv, D, causal, scale, static_cast<int>(dtype), gs, stream) == 0)
+    return ATTN_OK;
   // D = 16 / 32 at any length, and D = 64 with at most 64 queries and 256
   // keys: 64-row warp-level tensor-core tiles instead of 128-row tcgen05
   // tiles.
-  if (mid_kernel_takes(Sq, Skv, D, static_cast<int>(dtype))) {
-    const int r = launch_attn_mid(q, k, v, out, B, H, Sq, Skv, D, causal, scale, static_cast<int>(dtype), gs, stream);
-    if (r != -2) return r == 0 ? ATTN_OK : ATTN_ERR_LAUNCH;
-  }
+  if (mid_kernel_takes(Sq, Skv, D, static_cast<int>(dtype)) &&
+      launch_attn_mid(q, k, v, out, B, H, Sq, Skv, D, causal, scale, static_cast<int>(dtype), gs, stream) == 0)
+    return ATTN_OK;
   // The tensor-core kernel takes fp16/bf16 with D in {64, 128} and buffers
   // TMA can describe (16-byte aligned base and strides); every other call
   // runs the general kernel.
@@ -931,7 +942,11 @@ extern "C" int attn_get_status(cudaStream_t stream, int* status) {
   return ATTN_OK;
 }
 
-extern "C" int attn_library_version(void) { return 100; }
+extern "C" unsigned long long attn_set_wait_limit_ns(unsigned long long ns) {
+  return ra::g_wait_limit_ns.exchange(ns);
+}
+
+extern "C" int attn_library_version(void) { return 200; }
 
 #ifdef RA_TRACE
 // Trace builds only: selects the traced CTA and copies the timeline out.

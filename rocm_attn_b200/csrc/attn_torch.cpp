@@ -103,4 +103,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("k"), py::arg("v"), py::arg("causal") = false, py::arg("scale") = -1.0);
   m.def("check_status", &check_status, "Read and clear the kernel watchdog status", py::arg("device") = 0);
   m.def("library_version", &attn_library_version);
+  m.def("set_wait_limit_ns", [](uint64_t ns) { return static_cast<uint64_t>(attn_set_wait_limit_ns(ns)); },
+        "Limit of each pipeline wait of the tensor-core kernel for later launches (0: default 2 s); returns the "
+        "previous value. For tests of the watchdog path.",
+        py::arg("ns"));
 }

@@ -83,17 +83,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Waits until the phase with the given parity has completed.  Returns false
-// if the wait timed out (the status word gets `code`) or if another role of
-// this CTA already aborted.
+// if the wait took longer than `limit_ns` (the status word gets `code`) or if
+// another role of this CTA already aborted.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                          int* status, int code) {
+                                          int* status, int code, uint64_t limit_ns = kWaitTimeoutNs) {
   const uint32_t a = smem_addr(bar);
   if (mbar_try_wait(a, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   while (true) {
     if (mbar_try_wait(a, parity)) return true;
     if (*abort_flag) return false;
-    if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+    if (global_timer_ns() - t0 > limit_ns) {
       *abort_flag = 1;
       atomicCAS(status, 0, code);
       return false;
@@ -119,7 +119,8 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
-// 3-D tile store shared -> global; out-of-range rows are clipped by the unit.
+// 4-D tile load global -> shared (coordinates innermost first), completion
+// signalled on `bar` as tx bytes; rows outside the tensor are zero-filled.
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
                                             int c2, int c3, uint64_t cache_policy) {
   asm volatile(

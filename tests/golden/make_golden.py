@@ -13,7 +13,7 @@ Also stores the reference's own test inputs: the seeded cases of
 python/test/test_torch_interface.py:10-36 and the ramp known-answer case of
 src/tests/attn_test.cpp:52-60.
 
-    python tests/golden/make_golden.py [/path/to/reference]
+    python tests/golden/make_golden.py [/path/to/reference]   (default: $ROCM_ATTN_REF)
 
 Run once where the reference checkout exists; the .npz files are committed.
 """
@@ -46,7 +46,11 @@ def bits(t):
 
 
 def main():
-    ref_dir = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+    import oracle
+    ref_dir = sys.argv[1] if len(sys.argv) > 1 else oracle.reference_dir()
+    if not ref_dir:
+        raise SystemExit("usage: make_golden.py /path/to/reference (or set ROCM_ATTN_REF)")
     ref = load_reference(ref_dir)
     cases = []
     # hot-path cases: fp16/bf16, D in {64, 128}, self and cross, causal and not

@@ -20,7 +20,8 @@ ATTN_OK, ATTN_ERR_INVALID_ARGUMENT, ATTN_ERR_UNSUPPORTED, ATTN_ERR_MISALIGNED = 
 
 def declared_symbols():
     text = open(HEADER).read()
-    return re.findall(r"ATTN_API\s+\w+\s+(\w+)\s*\(", text)
+    # return types may be several words ("unsigned long long")
+    return re.findall(r"ATTN_API\s+(?:\w+\s+)+?\**(\w+)\s*\(", text)
 
 
 @pytest.fixture(scope="module")
@@ -53,7 +54,16 @@ def test_dtype_enum_matches_reference_values():
 
 
 def test_version(lib):
-    assert lib.attn_library_version() == 100
+    assert lib.attn_library_version() == 200
+
+
+def test_wait_limit_setter_round_trips(lib):
+    # a host-side setting only: no CUDA call, nothing launched
+    lib.attn_set_wait_limit_ns.argtypes = [ctypes.c_ulonglong]
+    lib.attn_set_wait_limit_ns.restype = ctypes.c_ulonglong
+    assert lib.attn_set_wait_limit_ns(12345) == 0
+    assert lib.attn_set_wait_limit_ns(0) == 12345
+    assert lib.attn_set_wait_limit_ns(0) == 0
 
 
 def _call(lib, q=0x1000, k=0x1000, v=0x1000, o=0x1000, B=1, H=1, Sq=8, Skv=8, D=64, causal=False, scale=-1.0,
@@ -90,7 +100,7 @@ def test_bindings_load_and_check_devices():
 
     assert rocm_attn_op.attn_forward is rocm_attn_b200.attn_forward
     import rocm_attn_op.rocm_attn_ext as ext  # the reference's module path keeps working
-    assert ext.library_version() == 100
+    assert ext.library_version() == 200
     x = torch.zeros(1, 1, 8, 64, dtype=torch.float16)
     with pytest.raises(RuntimeError, match="CUDA"):
         rocm_attn_op.attn_forward(x, x, x)

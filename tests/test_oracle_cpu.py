@@ -17,14 +17,11 @@ import torch
 import oracle
 from golden_util import cases, load
 
-REF_DIR = "/root/reference"
-
-
 def test_reference_known_answer_test():
     if not os.path.exists(oracle.REF_KAT_BIN):
-        if not os.path.isdir(REF_DIR):
+        if not oracle.reference_dir():
             pytest.skip("reference sources absent and the known-answer binary was not built")
-        oracle.build(REF_DIR)
+        oracle.build()
     ok, out = oracle.run_reference_kat()
     assert ok, out
 

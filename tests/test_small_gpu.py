@@ -32,6 +32,15 @@ def test_small_shapes(attn, sq, skv, d, causal, dtype):
     _check(attn, Shape(3, 5, sq, skv, d), dtype, causal, seed=sq * 100 + skv)
 
 
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("sq,skv", [(1, 64), (8, 40), (8, 17), (8, 16), (3, 64)])
+def test_fp32_d128_decode_shapes(attn, sq, skv, causal):
+    # fp32 at D = 128 with 17-64 keys: the SIMT short kernel's fp32 K and V would
+    # need 256 KiB of shared memory, so the dispatcher sends these to the
+    # general kernel; with up to 16 keys the SIMT kernel takes them.
+    _check(attn, Shape(2, 3, sq, skv, 128), torch.float32, causal, seed=sq * 1000 + skv)
+
+
 @pytest.mark.parametrize("idx", [0, 2, 4, 6, 8])
 def test_unifolm_short_shapes(attn, idx):
     s = WORKLOADS["unifolm"].shapes[idx]
