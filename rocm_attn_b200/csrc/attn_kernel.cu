@@ -278,11 +278,13 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles, kBlockKeys>::kThreads, Cfg<kD,
   const uint32_t tmem = ctl.tmem_base;
 
   RA_MARK(8190 - warp);
+  // The last block loaded into each K / V stage (TMA warp; block 0 was issued
+  // during setup), for the drain of an aborted CTA.
+  int last_k[3] = {0, -1, -1}, last_v[3] = {0, -1, -1};
   if (warp == C::kTmaWarp) {
     // ------------------------------------------------------------------ TMA
     const uint64_t pol_keep = l2_policy_evict_last();
     const bool leader = elect_one();
-    int last_k[3] = {0, -1, -1}, last_v[3] = {0, -1, -1};  // block 0 was issued during setup
     bool ok = true;
     for (int j = 1; j < nkb && ok; ++j) {
       const int sk = j % C::kStagesK;
@@ -310,16 +312,6 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles, kBlockKeys>::kThreads, Cfg<kD,
       }
       last_v[sv] = j;
       RA_MARK(6144 + j * 4 + 2);
-    }
-    if (!ok) {
-      // Aborted: let every copy already issued land before the CTA exits.
-      volatile int no_abort = 0;
-      mbar_wait(&ctl.q_full[0], 0, &no_abort, status, kWatchDrain);
-      if (n1 > 0) mbar_wait(&ctl.q_full[1], 0, &no_abort, status, kWatchDrain);
-      for (int s = 0; s < 3; ++s) {
-        if (last_k[s] >= 0) mbar_wait(&ctl.k_full[s], (last_k[s] / C::kStagesK) & 1, &no_abort, status, kWatchDrain);
-        if (last_v[s] >= 0) mbar_wait(&ctl.v_full[s], (last_v[s] / C::kStagesV) & 1, &no_abort, status, kWatchDrain);
-      }
     }
   } else if (warp == C::kMmaWarp) {
     // ------------------------------------------------------------------ UMMA
@@ -706,6 +698,19 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles, kBlockKeys>::kThreads, Cfg<kD,
   RA_MARK(8180 - warp);
   tc_fence_before();
   __syncthreads();
+  if (warp == C::kTmaWarp && *abort_flag) {
+    // Some role gave up on a wait (every role has finished by now, so the flag
+    // is final): let every copy already issued land before the CTA exits,
+    // also when this warp itself had issued all its blocks.  Without an abort
+    // every issued block was consumed, so there is nothing to wait for.
+    volatile int no_abort = 0;
+    mbar_wait(&ctl.q_full[0], 0, &no_abort, status, kWatchDrain);
+    if (n1 > 0) mbar_wait(&ctl.q_full[1], 0, &no_abort, status, kWatchDrain);
+    for (int s = 0; s < 3; ++s) {
+      if (last_k[s] >= 0) mbar_wait(&ctl.k_full[s], (last_k[s] / C::kStagesK) & 1, &no_abort, status, kWatchDrain);
+      if (last_v[s] >= 0) mbar_wait(&ctl.v_full[s], (last_v[s] / C::kStagesV) & 1, &no_abort, status, kWatchDrain);
+    }
+  }
   if (warp == C::kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, C::kTmemCols);
