@@ -99,12 +99,14 @@ ATTN_API int attn_get_status(cudaStream_t stream, int* status);
 /*
  * Sets the limit, in nanoseconds, of each pipeline wait inside the
  * tensor-core kernel for launches queued from now on (all devices); 0 restores
- * the default of 2 s.  A legitimate wait lasts microseconds, so the limit only
- * expires when an arrival was lost: the kernel then records ATTN_ERR_WATCHDOG
- * (read with attn_get_status), lets the copies and products it already issued
- * finish under the default limit, frees its tensor memory and returns.  Meant
- * for tests of that path; returns the previous limit (0 = default).  No
- * counterpart in the reference, whose kernels have no bounded waits.
+ * the default of 2 s.  The clock is checked each time the hardware's own
+ * suspension of an mbarrier wait ends without the awaited arrival, so a
+ * legitimate wait (microseconds) never expires whatever the limit, and a
+ * lost arrival ends the wait after about the limit: the kernel then records
+ * ATTN_ERR_WATCHDOG (read with attn_get_status), lets the copies and products
+ * it already issued finish under the default limit, frees its tensor memory
+ * and returns.  Returns the previous limit (0 = default).  No counterpart in
+ * the reference, whose kernels have no bounded waits.
  */
 ATTN_API unsigned long long attn_set_wait_limit_ns(unsigned long long ns);
 

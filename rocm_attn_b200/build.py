@@ -5,6 +5,8 @@
   ``csrc/attn_general.cu``: fp32 / other head dims), compiled by nvcc for
   ``sm_100a`` only, with the
   CUDA runtime linked statically so the library loads without torch.
+* ``librocm_attn_wdtest.so`` -- the same kernels built with
+  RA_WATCHDOG_TEST for the watchdog's GPU test (see WATCHDOG_TEST_LIB).
 * ``rocm_attn_ext*.so`` -- the PyTorch binding (``csrc/attn_torch.cpp``),
   linked against ``librocm_attn.so`` through an ``$ORIGIN`` rpath.
 
@@ -52,16 +54,43 @@ def _kernel_sources() -> list[str]:
             if f.endswith((".cu", ".cuh", ".h"))] + [os.path.join(INCLUDE, "attn_kernel.h")]
 
 
+# The watchdog test build: the same sources with RA_WATCHDOG_TEST, which can
+# lose one pipeline arrival on request so that a GPU test can make a wait run
+# out (tests/test_watchdog_gpu.py).  Never loaded by the package.
+WATCHDOG_TEST_LIB = os.path.join(PKG_DIR, "librocm_attn_wdtest.so")
+OBJ_DIR = os.path.join(PKG_DIR, "_build", "kernels")
+
+
+def _compile(src: str, obj: str, defines=(), verbose: bool = False) -> str:
+    if _newer(obj, _kernel_sources()):
+        os.makedirs(os.path.dirname(obj), exist_ok=True)
+        cmd = [_nvcc(), *NVCC_FLAGS, *(f"-D{d}" for d in defines), "-I", INCLUDE, "-c", src, "-o", obj + ".tmp"]
+        if verbose:
+            cmd.insert(1, "-Xptxas=-v")
+        subprocess.run(cmd, check=True)
+        os.replace(obj + ".tmp", obj)
+    return obj
+
+
+def _link(objs: list[str], lib: str) -> None:
+    subprocess.run([_nvcc(), *NVCC_FLAGS, "-shared", *objs, "-o", lib + ".tmp"], check=True)
+    os.replace(lib + ".tmp", lib)
+
+
 def build_kernel_lib(force: bool = False, verbose: bool = False) -> str:
-    """Compile csrc/*.cu into librocm_attn.so (sm_100a)."""
-    if not force and not _newer(KERNEL_LIB, _kernel_sources()):
-        return KERNEL_LIB
-    cmd = [_nvcc(), *NVCC_FLAGS, "-I", INCLUDE, "-shared",
-           os.path.join(CSRC, "attn_kernel.cu"), os.path.join(CSRC, "attn_general.cu"), "-o", KERNEL_LIB + ".tmp"]
-    if verbose:
-        cmd.insert(1, "-Xptxas=-v")
-    subprocess.run(cmd, check=True)
-    os.replace(KERNEL_LIB + ".tmp", KERNEL_LIB)
+    """Compile csrc/*.cu into librocm_attn.so (sm_100a), and the watchdog
+    test build of the same sources into librocm_attn_wdtest.so."""
+    if force or _newer(KERNEL_LIB, _kernel_sources()) or _newer(WATCHDOG_TEST_LIB, _kernel_sources()):
+        if force and os.path.isdir(OBJ_DIR):
+            shutil.rmtree(OBJ_DIR)
+        general = _compile(os.path.join(CSRC, "attn_general.cu"), os.path.join(OBJ_DIR, "attn_general.o"),
+                           verbose=verbose)
+        kernel = _compile(os.path.join(CSRC, "attn_kernel.cu"), os.path.join(OBJ_DIR, "attn_kernel.o"),
+                          verbose=verbose)
+        _link([kernel, general], KERNEL_LIB)
+        wd = _compile(os.path.join(CSRC, "attn_kernel.cu"), os.path.join(OBJ_DIR, "attn_kernel_wdtest.o"),
+                      defines=("RA_WATCHDOG_TEST",))
+        _link([wd, general], WATCHDOG_TEST_LIB)
     return KERNEL_LIB
 
 

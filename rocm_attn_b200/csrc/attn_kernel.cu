@@ -84,6 +84,7 @@ struct AttnParams {
   int head_group;   // causal: heads per scheduling group (their K/V fit in L2)
   float scale_log2; // softmax scale * log2(e)
   unsigned long long wait_ns;  // limit of every pipeline wait (the watchdog)
+  int drop_arrival;            // watchdog test build only: lose one P arrival of CTA 0
 };
 
 // Compile-time shape of the pipeline for head dimension kD, kTiles 128-row
@@ -513,6 +514,12 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles, kBlockKeys>::kThreads, Cfg<kD,
       tc_fence_before();
       mbar_arrive(&ctl.p_full[t][h]);
     };
+#ifdef RA_WATCHDOG_TEST
+    // Watchdog test build: when the launch asks for it, CTA 0's tile 0 loses
+    // its first P arrival (half 0 of block 0).  Nothing else ever completes
+    // that phase, so the MMA warp's wait for it can only end by the watchdog.
+    const bool drop_first = p.drop_arrival != 0 && blockIdx.x == 0 && t == 0;
+#endif
 
     // Loads the block's kBN fp32 scores of this thread's row and masks keys
     // past Lk and, when causal, keys after the query.
@@ -629,6 +636,9 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles, kBlockKeys>::kThreads, Cfg<kD,
           tc_fence_after();
         }
       }
+#ifdef RA_WATCHDOG_TEST
+      if (!(drop_first && j == 0))  // lost: neither stored nor signalled
+#endif
       store_half(0, pk);
       RA_MARK(t * 2048 + j * 16 + 5);
       {
@@ -730,6 +740,9 @@ struct Strides {
 // Pipeline wait limit for launches from now on (attn_set_wait_limit_ns);
 // 0 selects kWaitTimeoutNs.
 static std::atomic<unsigned long long> g_wait_limit_ns{0};
+#ifdef RA_WATCHDOG_TEST
+static std::atomic<int> g_drop_arrival{0};
+#endif
 
 // Returned by launch_impl when a buffer or stride cannot be described to TMA
 // (the caller then runs the general kernel).
@@ -792,6 +805,11 @@ static int launch_impl(const void* q, const void* k, const void* v, void* out, i
   prm.scale_log2 = scale * 1.4426950408889634f;
   const unsigned long long limit = g_wait_limit_ns.load(std::memory_order_relaxed);
   prm.wait_ns = limit != 0 ? limit : kWaitTimeoutNs;
+#ifdef RA_WATCHDOG_TEST
+  prm.drop_arrival = g_drop_arrival.load(std::memory_order_relaxed);
+#else
+  prm.drop_arrival = 0;
+#endif
   const long long grid = static_cast<long long>(prm.num_qblocks) * BH;
   if (grid > 0x7fffffffLL) return ATTN_ERR_INVALID_ARGUMENT;
   kern<<<static_cast<unsigned>(grid), C::kThreads, C::kSmemBytes, stream>>>(mq, mk, mv, mo, prm);
@@ -952,6 +970,13 @@ extern "C" unsigned long long attn_set_wait_limit_ns(unsigned long long ns) {
 }
 
 extern "C" int attn_library_version(void) { return 200; }
+
+#ifdef RA_WATCHDOG_TEST
+// Watchdog test build only (librocm_attn_wdtest.so, never the product
+// library): with `on` set, every later tensor-core launch loses one P arrival
+// in CTA 0, so that its wait can only end by the watchdog.
+extern "C" ATTN_API void attn_test_drop_arrival(int on) { ra::g_drop_arrival.store(on); }
+#endif
 
 #ifdef RA_TRACE
 // Trace builds only: selects the traced CTA and copies the timeline out.
