@@ -88,6 +88,38 @@ ATTN_API int launch_attn_forward_strided(const void* q, const void* k, const voi
                                          const long long* v_strides, cudaStream_t stream);
 
 /*
+ * One problem of launch_attn_forward_batch: the arguments of
+ * launch_attn_forward_strided for one call (null strides: contiguous).
+ */
+typedef struct AttnProblem {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* out;
+  int B, H, Sq, Skv, D;
+  bool causal;
+  float softmax_scale;
+  const long long* q_strides;
+  const long long* k_strides;
+  const long long* v_strides;
+} AttnProblem;
+
+/*
+ * Runs n independent problems of one dtype, as launch_attn_forward_strided
+ * would one by one, with the same results bit for bit, in fewer launches:
+ * the problems that run the tcgen05 tensor-core kernel with the same head
+ * dim, masking and tile shape share one grid (up to 16 problems per grid),
+ * whose work units are ordered longest first, so the short units of one
+ * problem fill the last wave of another and no launch waits for the tail of
+ * the previous one.  The others are launched one by one.  Every problem is
+ * checked before anything is launched; on an error nothing was launched.
+ * The output buffers must not overlap any input or each other.  No
+ * counterpart in the reference, whose benchmark launches one shape at a time
+ * (benchmark/bench_attention.py:81-100,171-175).
+ */
+ATTN_API int launch_attn_forward_batch(const AttnProblem* problems, int n, AttnDType dtype, cudaStream_t stream);
+
+/*
  * Reads and clears the device status word of the current device, after
  * synchronising `stream`.  *status receives ATTN_OK, or ATTN_ERR_WATCHDOG when a
  * kernel launched earlier gave up on a wait (its output is then invalid).

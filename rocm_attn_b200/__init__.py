@@ -13,7 +13,7 @@ from __future__ import annotations
 import importlib.util
 import os
 import sysconfig
-from typing import Optional
+from typing import Optional, Sequence
 
 import torch
 
@@ -58,6 +58,18 @@ def attn_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool
     return rocm_attn_ext.attn_forward(q, k, v, bool(causal), -1.0 if scale is None else float(scale))
 
 
+def attn_forward_batch(qs: Sequence[torch.Tensor], ks: Sequence[torch.Tensor], vs: Sequence[torch.Tensor],
+                       causal: bool = False, scale: Optional[float] = None) -> list:
+    """Several independent attention problems (e.g. a sequence of shapes) in
+    one call: returns ``[attn_forward(q, k, v, causal, scale) for ...]``, the
+    same values bit for bit, with the problems that run the tcgen05 kernel at
+    the same head dim and tile shape sharing one grid (longest units first),
+    so they pay one launch and one partial last wave instead of one each.
+    All problems share dtype, device, ``causal`` and ``scale``."""
+    return list(rocm_attn_ext.attn_forward_batch(list(qs), list(ks), list(vs), bool(causal),
+                                                 -1.0 if scale is None else float(scale)))
+
+
 def check_status(device: int = 0) -> int:
     """Synchronise ``device`` and return (and clear) the kernel watchdog
     status: 0 when every earlier launch completed, non-zero when a kernel gave
@@ -67,5 +79,5 @@ def check_status(device: int = 0) -> int:
 
 from .pipeline import attn_forward_pinned  # noqa: E402  (host-resident inputs, transfers overlapped)
 
-__all__ = ["attn_forward", "attn_forward_pinned", "check_status", "rocm_attn_ext", "KERNEL_LIB_PATH",
+__all__ = ["attn_forward", "attn_forward_batch", "attn_forward_pinned", "check_status", "rocm_attn_ext", "KERNEL_LIB_PATH",
            "SUPPORTED_HEAD_DIMS", "SUPPORTED_DTYPES", "MAX_HEAD_DIM"]

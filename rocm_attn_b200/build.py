@@ -2,6 +2,7 @@
 
 * ``librocm_attn.so``  -- the sm_100a kernels and the C-ABI launcher
   (``csrc/attn_kernel.cu``: tensor-core kernel and dispatch;
+  ``csrc/attn_group.cu``: grouped launches of several problems;
   ``csrc/attn_general.cu``: fp32 / other head dims), compiled by nvcc for
   ``sm_100a`` only, with the
   CUDA runtime linked statically so the library loads without torch.
@@ -20,6 +21,7 @@ import shutil
 import subprocess
 import sys
 import sysconfig
+from concurrent.futures import ThreadPoolExecutor
 
 PKG_DIR = os.path.dirname(os.path.abspath(__file__))
 REPO_DIR = os.path.dirname(PKG_DIR)
@@ -61,8 +63,24 @@ WATCHDOG_TEST_LIB = os.path.join(PKG_DIR, "librocm_attn_wdtest.so")
 OBJ_DIR = os.path.join(PKG_DIR, "_build", "kernels")
 
 
+def _deps(src: str) -> list[str]:
+    """The source and the local headers it includes, transitively."""
+    seen, todo = [], [src]
+    while todo:
+        f = todo.pop()
+        if f in seen or not os.path.exists(f):
+            continue
+        seen.append(f)
+        for line in open(f):
+            line = line.strip()
+            if line.startswith('#include "'):
+                name = line.split('"')[1]
+                todo += [os.path.join(CSRC, name), os.path.join(INCLUDE, name)]
+    return seen
+
+
 def _compile(src: str, obj: str, defines=(), verbose: bool = False) -> str:
-    if _newer(obj, _kernel_sources()):
+    if _newer(obj, _deps(src)):
         os.makedirs(os.path.dirname(obj), exist_ok=True)
         cmd = [_nvcc(), *NVCC_FLAGS, *(f"-D{d}" for d in defines), "-I", INCLUDE, "-c", src, "-o", obj + ".tmp"]
         if verbose:
@@ -83,14 +101,16 @@ def build_kernel_lib(force: bool = False, verbose: bool = False) -> str:
     if force or _newer(KERNEL_LIB, _kernel_sources()) or _newer(WATCHDOG_TEST_LIB, _kernel_sources()):
         if force and os.path.isdir(OBJ_DIR):
             shutil.rmtree(OBJ_DIR)
-        general = _compile(os.path.join(CSRC, "attn_general.cu"), os.path.join(OBJ_DIR, "attn_general.o"),
-                           verbose=verbose)
-        kernel = _compile(os.path.join(CSRC, "attn_kernel.cu"), os.path.join(OBJ_DIR, "attn_kernel.o"),
-                          verbose=verbose)
-        _link([kernel, general], KERNEL_LIB)
-        wd = _compile(os.path.join(CSRC, "attn_kernel.cu"), os.path.join(OBJ_DIR, "attn_kernel_wdtest.o"),
-                      defines=("RA_WATCHDOG_TEST",))
-        _link([wd, general], WATCHDOG_TEST_LIB)
+        # The translation units compile in parallel (each takes about a minute).
+        jobs = [("attn_general.cu", "attn_general.o", ()), ("attn_kernel.cu", "attn_kernel.o", ()),
+                ("attn_group.cu", "attn_group.o", ()),
+                ("attn_kernel.cu", "attn_kernel_wdtest.o", ("RA_WATCHDOG_TEST",))]
+        with ThreadPoolExecutor(len(jobs)) as ex:
+            general, kernel, group, wd = ex.map(
+                lambda j: _compile(os.path.join(CSRC, j[0]), os.path.join(OBJ_DIR, j[1]), defines=j[2],
+                                   verbose=verbose), jobs)
+        _link([kernel, group, general], KERNEL_LIB)
+        _link([wd, group, general], WATCHDOG_TEST_LIB)
     return KERNEL_LIB
 
 

@@ -7,8 +7,8 @@ to the sm_100a implementation in ``rocm_attn_b200``.
 """
 import sys as _sys
 
-from rocm_attn_b200 import attn_forward, check_status, rocm_attn_ext
+from rocm_attn_b200 import attn_forward, attn_forward_batch, check_status, rocm_attn_ext
 
 _sys.modules[__name__ + ".rocm_attn_ext"] = rocm_attn_ext
 
-__all__ = ["attn_forward", "check_status", "rocm_attn_ext"]
+__all__ = ["attn_forward", "attn_forward_batch", "check_status", "rocm_attn_ext"]
