@@ -90,6 +90,34 @@ def test_argument_checks_before_any_cuda_call(lib):
     assert _call(lib, Sq=0) == ATTN_OK
 
 
+class _AttnProblem(ctypes.Structure):
+    _fields_ = [("q", ctypes.c_void_p), ("k", ctypes.c_void_p), ("v", ctypes.c_void_p), ("out", ctypes.c_void_p),
+                ("B", ctypes.c_int), ("H", ctypes.c_int), ("Sq", ctypes.c_int), ("Skv", ctypes.c_int),
+                ("D", ctypes.c_int), ("causal", ctypes.c_bool), ("softmax_scale", ctypes.c_float),
+                ("q_strides", ctypes.c_void_p), ("k_strides", ctypes.c_void_p), ("v_strides", ctypes.c_void_p)]
+
+
+def test_batch_argument_checks_before_any_cuda_call(lib):
+    # The batch entry checks every problem before launching any; these fail
+    # (or finish) before the device is touched.  The pointers are fake.
+    lib.launch_attn_forward_batch.argtypes = [ctypes.POINTER(_AttnProblem), ctypes.c_int, ctypes.c_int,
+                                              ctypes.c_void_p]
+    lib.launch_attn_forward_batch.restype = ctypes.c_int
+    good = _AttnProblem(0x1000, 0x1000, 0x1000, 0x1000, 0, 1, 8, 8, 64, False, -1.0, None, None, None)  # empty
+    bad_d = _AttnProblem(0x1000, 0x1000, 0x1000, 0x1000, 1, 1, 8, 8, 1000, False, -1.0, None, None, None)
+    bad_ptr = _AttnProblem(None, 0x1000, 0x1000, 0x1000, 1, 1, 8, 8, 64, False, -1.0, None, None, None)
+    arr = (_AttnProblem * 3)(good, bad_d, good)
+    assert lib.launch_attn_forward_batch(arr, 3, 0, None) == ATTN_ERR_UNSUPPORTED
+    arr = (_AttnProblem * 2)(good, bad_ptr)
+    assert lib.launch_attn_forward_batch(arr, 2, 0, None) == ATTN_ERR_INVALID_ARGUMENT
+    assert lib.launch_attn_forward_batch(None, 1, 0, None) == ATTN_ERR_INVALID_ARGUMENT
+    assert lib.launch_attn_forward_batch(None, -1, 0, None) == ATTN_ERR_INVALID_ARGUMENT
+    assert lib.launch_attn_forward_batch(None, 0, 0, None) == ATTN_OK
+    arr = (_AttnProblem * 2)(good, good)
+    assert lib.launch_attn_forward_batch(arr, 2, 0, None) == ATTN_OK  # only empty problems
+    assert lib.launch_attn_forward_batch(arr, 2, 9, None) == ATTN_ERR_UNSUPPORTED  # unknown dtype
+
+
 def test_status_requires_output_pointer(lib):
     assert lib.attn_get_status(None, None) == ATTN_ERR_INVALID_ARGUMENT
 
