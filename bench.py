@@ -458,14 +458,28 @@ def per_config_table(args, dev, stream, flush, headline: dict):
                         "hbm_gbs": round(byts / (ms * 1e-3) / 1e9, 1),
                         "frac_of_measured_hbm": round(byts / (ms * 1e-3) / 1e9 / hbm, 4)})
             if len(w.shapes) > 1:
-                graph = torch.cuda.CUDAGraph()
-                ours()
+                # the same sequence as one call of the batch entry point
+                # (grouped tensor-core grids), and both sequences replayed
+                # from CUDA graphs; the batch must equal the per-shape calls
+                def batched():
+                    return rocm_attn_op.attn_forward_batch([t[0] for t in inputs], [t[1] for t in inputs],
+                                                           [t[2] for t in inputs], causal=w.causal)
+
+                bms = statistics.median(time_steps(batched, steps, args.warmup, flush, stream))
+                a, b = ours(), batched()
                 torch.cuda.synchronize()
-                with torch.cuda.graph(graph):
-                    ours()
-                gms = statistics.median(time_steps(graph.replay, steps, args.warmup, flush, stream))
-                row["graph_ms"] = round(gms, 4)
-                del graph
+                row["batch"] = {"ms": round(bms, 4), "tflops": round(w.flops() / (bms * 1e-3) / 1e12, 2),
+                                "equal_to_per_shape_calls": all(torch.equal(x, y) for x, y in zip(a, b))}
+                del a, b
+                for name, fn in (("graph_ms", ours), ("batch_graph_ms", batched)):
+                    graph = torch.cuda.CUDAGraph()
+                    fn()
+                    torch.cuda.synchronize()
+                    with torch.cuda.graph(graph):
+                        fn()
+                    gms = statistics.median(time_steps(graph.replay, steps, args.warmup, flush, stream))
+                    row[name] = round(gms, 4)
+                    del graph
             if reuse and headline.get("parity") is not None:
                 row["parity"] = headline["parity"]
             elif not args.no_parity:
