@@ -14,12 +14,26 @@ from __future__ import annotations
 
 import math
 import threading
+from collections import OrderedDict
 from typing import Optional
 
 import torch
 
 _lock = threading.Lock()
-_state: dict = {}
+_state: "OrderedDict[tuple, dict]" = OrderedDict()
+# Device buffer sets kept for reuse (the most recently used ones); a caller
+# cycling through more shapes than this reallocates, but memory stays bounded.
+MAX_CACHED_SHAPES = 4
+
+
+def _release(st: dict) -> None:
+    """Waits until no queued work can still touch the buffers of an evicted
+    entry (its copies and the attention launches that read them), so the
+    allocator may hand the memory to someone else."""
+    for ev in st["done"].values():
+        ev.synchronize()
+    st["s_in"].synchronize()
+    st["s_out"].synchronize()
 
 
 def _device_state(device: torch.device, key: tuple, q_shape, k_shape, dtype):
@@ -27,7 +41,12 @@ def _device_state(device: torch.device, key: tuple, q_shape, k_shape, dtype):
     reused across calls so a steady caller allocates nothing."""
     with _lock:
         st = _state.get(key)
-        if st is None:
+        if st is not None:
+            _state.move_to_end(key)
+        else:
+            while len(_state) >= MAX_CACHED_SHAPES:
+                _, old = _state.popitem(last=False)
+                _release(old)
             st = {
                 "q": torch.empty(q_shape, dtype=dtype, device=device),
                 "k": torch.empty(k_shape, dtype=dtype, device=device),
@@ -52,11 +71,15 @@ def attn_forward_pinned(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causa
     33 MB to 805 MB of inputs, where every chunk adds some host work)."""
     from . import attn_forward
 
-    if device is None:
-        device = torch.device("cuda", torch.cuda.current_device())
-    for t in (q, k, v):
+    for t in (q, k, v) + ((out,) if out is not None else ()):
         if t.device.type != "cpu" or not t.is_contiguous():
             raise ValueError("attn_forward_pinned takes contiguous host tensors")
+        if not t.is_pinned():
+            # a pageable buffer turns every chunk copy into a synchronous
+            # staged copy, which defeats the overlap this entry point exists for
+            raise ValueError("attn_forward_pinned takes pinned host tensors (use .pin_memory())")
+    if device is None:
+        device = torch.device("cuda", torch.cuda.current_device())
     B, H, Lq, D = q.shape
     Lk = k.shape[2]
     BH = B * H
@@ -105,4 +128,4 @@ def attn_forward_pinned(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causa
     return out
 
 
-__all__ = ["attn_forward_pinned"]
+__all__ = ["attn_forward_pinned", "MAX_CACHED_SHAPES"]

@@ -29,3 +29,14 @@ def test_pinned_matches_device_op(attn, shape, dtype, causal, chunk):
     out2 = attn.attn_forward_pinned(q2, k, v, causal=causal, chunk_slices=chunk)
     torch.cuda.synchronize()
     assert torch.equal(out2, attn.attn_forward(q2.cuda(), k.cuda(), v.cuda(), causal=causal).cpu())
+
+
+def test_pinned_buffer_cache_is_bounded(attn):
+    from rocm_attn_b200 import pipeline
+    shapes = [Shape(1, 2, 64 + 32 * i, 64 + 32 * i, 64) for i in range(pipeline.MAX_CACHED_SHAPES + 3)]
+    for s in shapes:
+        q, k, v = (t.contiguous().pin_memory() for t in make_qkv(s, torch.float16, seed=1))
+        out = attn.attn_forward_pinned(q, k, v)
+        torch.cuda.synchronize()
+        assert torch.equal(out, attn.attn_forward(q.cuda(), k.cuda(), v.cuda()).cpu())
+        assert len(pipeline._state) <= pipeline.MAX_CACHED_SHAPES

@@ -56,3 +56,12 @@ def test_local_view_is_a_view():
     t = torch.arange(2 * 3 * 4 * 8, dtype=torch.float32).view(2, 3, 4, 8)
     v = local_view(t, 4, 1)
     assert v.shape == (1, 2, 4, 8) and v.data_ptr() == t[0, 1].data_ptr()
+
+
+def test_pinned_entry_rejects_pageable_tensors():
+    # checked before any CUDA call, so this runs without a GPU
+    import pytest
+    import rocm_attn_b200
+    x = torch.zeros(1, 1, 8, 64, dtype=torch.float16)
+    with pytest.raises(ValueError, match="pinned"):
+        rocm_attn_b200.attn_forward_pinned(x, x, x)
