@@ -39,6 +39,7 @@ Reported on the line:
                 reference's _sdpa_fallback runs it) on the host cores, fp32,
                 on a bounded sample of the same workload's heads
   clocks        NVML samples taken during the timed region
+  --nvtx        one NVTX range per shape launch, for profiler timelines
   gather        N > 1 only: the NCCL all-gather that assembles the full O
                 on every rank, timed on its own after the timed region
 ``--impl reference`` times that CPU reference path alone on the same
@@ -109,6 +110,9 @@ def parse_args(argv=None):
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-per-config", action="store_true", help="skip the per-configuration table (N=1)")
     ap.add_argument("--no-parity", action="store_true", help="skip the oracle check of the timed inputs")
+    ap.add_argument("--nvtx", action="store_true",
+                    help="wrap every shape's launch in an NVTX range named after the shape (for nsys/ncu timelines); "
+                         "host-side only, off by default")
     ap.add_argument("--graph", action="store_true",
                     help="capture one step (all shapes of the workload) in a CUDA graph and time its replays: "
                          "removes the per-launch host overhead of small-shape workloads")
@@ -518,11 +522,19 @@ def run_ours(args, rank, world, local_rank):
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
     dist = torch.distributed if world > 1 else None
 
+    names = [f"attn {s.B}x{s.H}x{s.Lq}x{s.Lk}x{s.D}{' causal' if w.causal else ''} rows {r.start}-{r.stop}"
+             for s, r in shards]
+
     def step():
         outs = []
-        for t in inputs:
-            if t is not None:
-                outs.append(rocm_attn_op.attn_forward(t[0], t[1], t[2], causal=w.causal))
+        for t, name in zip(inputs, names):
+            if t is None:
+                continue
+            if args.nvtx:
+                torch.cuda.nvtx.range_push(name)
+            outs.append(rocm_attn_op.attn_forward(t[0], t[1], t[2], causal=w.causal))
+            if args.nvtx:
+                torch.cuda.nvtx.range_pop()
         return outs
 
     for _ in range(max(3, args.warmup)):
