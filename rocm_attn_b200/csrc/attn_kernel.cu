@@ -1,42 +1,15 @@
-// Fused attention forward for NVIDIA B200 (sm_100a): TMA -> shared memory ->
-// tcgen05 UMMA with accumulators in tensor memory, online softmax in base 2;
-// and the C-ABI entry points, whose dispatcher sends short, mid-length, fp32
-// and other-head-dim calls to the kernels of attn_general.cu.
+// C-ABI entry points of the attention-forward library and their dispatcher.
 //
-// Replaces the reference's HIP kernels and their launcher
-// (src/attn_kernel_torch.cu:36-689, src/attn_kernel.hip.cpp:36-367 of
-// JoursBleu/rocm_attn).  The math is the reference's: per query row,
-// s_j = (q . k_j) * scale, masked when causal and j > i
-// (src/attn_kernel_torch.cu:54,238,263), softmax in the exp2 domain with a
-// running fp32 max and sum (src/attn_kernel_torch.cu:269-298), O = P V / sum
-// (src/attn_kernel_torch.cu:333-354).
-//
-// CTA work unit.  D=128: 256 query rows of one (batch, head) as two 128-row
-// Q tiles, one CTA per SM.  D=64: one 128-row tile, two CTAs per SM with
-// 128-key blocks, three with 64-key blocks (short key ranges).
-// Warp roles (320 threads with two tiles, 192 with one):
-//   warps 0-3  softmax of Q tile 0 (thread <-> TMEM lane <-> query row)
-//   warps 4-7  softmax of Q tile 1 (two-tile CTAs)
-//   next warp  UMMA issue (one elected lane) and TMEM allocation
-//   last warp  TMA producer for K/V blocks 1.. of 128 or 64 keys (thread 0 starts
-//              the Q tiles and block 0 during setup)
-// Tensor memory (128 lanes x 32 bit; 512 columns for two tiles, 256 or 128
-// for one):
-//   D=128: S0 [0,128) S1 [128,256) fp32 scores of the current key block;
-//          P0 = S0 cols [0,64), P1 = S1 cols [0,64) (16-bit, aliasing S);
-//          O0 [256,384) O1 [384,512) fp32 output accumulators
-//   D=64:  S [0,128), P [128,192) apart from S, O [192,256); with 64-key
-//          blocks S [0,64), P aliasing S cols [0,32), O [64,128)
-// UMMA issue order per key block j at D=128 (tcgen05.mma executes in issue
-// order):
-//   S0(j)=Q0 K_j^T, O1+=P1(j-1) V_{j-1}, S1(j)=Q1 K_j^T, O0+=P0(j) V_j
-// so each softmax warpgroup works while the tensor core runs the other tile;
-// at D=64 with 128-key blocks, S(j+1) is issued as soon as the softmax has
-// read S(j), and the other CTAs on the SM keep the tensor core busy meanwhile.
-// The running max is only moved (and O rescaled) when it grows by more than
-// 2^8 in the exp2 domain; P values stay <= 256, exact in fp16/bf16 range, and
-// the final division by the matching running sum makes the result identical
-// in exact arithmetic.
+// Replaces the reference's launcher (src/attn_kernel_torch.cu:625-689,
+// src/attn_kernel.hip.cpp:304-367 of JoursBleu/rocm_attn), which picks one of
+// its HIP kernels by head dim and shared-memory size.  Here `prepare` checks
+// a call and picks its route without queueing anything, and `run` launches
+// it: short sequences, mid-length sequences, fp32 and other head dims go to
+// the kernels of attn_general.cu; fp16/bf16 at D = 64 / 128 with buffers TMA
+// can describe go to the tcgen05 kernel of attn_fwd.cuh, one grid per call
+// (here) or several problems per grid (attn_group.cu, for
+// launch_attn_forward_batch).  Also: the watchdog's status word and limit,
+// and, in the watchdog test build only, the hook that loses one arrival.
 
 #include "attn_fwd.cuh"
 #include "attn_general.h"
