@@ -858,7 +858,8 @@ template <bool kBf16, int kD, bool kCausal, int kTiles, int kBlockKeys, int kMax
 int launch_fwd(const FwdArgs<kMaxProblems>& a, cudaStream_t stream) {
   using C = Cfg<kD, kTiles, kBlockKeys>;
   auto kern = attn_fwd_kernel<kBf16, kD, kCausal, kTiles, kBlockKeys, kMaxProblems>;
-  // Opt in to the large dynamic shared-memory carve-out once per device.
+  // Opt in to the large dynamic shared-memory carve-out once per device
+  // (under the mutex: launches may come from several host threads).
   static bool configured[64] = {};
   static std::mutex mu;
   int dev = 0;

@@ -46,15 +46,15 @@ static int launch_impl(const FwdProblem& d, cudaStream_t stream) {
 // Multiprocessor count of the current device, cached per device (0 if it
 // cannot be read).
 static int sm_count() {
-  static int cached[64] = {};
+  static std::atomic<int> cached[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
-  if (cached[dev] == 0) {
-    int n = 0;
+  int n = cached[dev].load(std::memory_order_relaxed);
+  if (n == 0) {
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
-    cached[dev] = n;
+    cached[dev].store(n, std::memory_order_relaxed);
   }
-  return cached[dev];
+  return n;
 }
 
 // D=64 problems for 64-key blocks: with few blocks per unit the fixed cost of
@@ -68,17 +68,19 @@ static bool d64_short_keys(long long ctas, int Skv, bool causal) {
 
 // Compute capability 10.x check, cached per device.
 static int check_device() {
-  static int cached[64] = {};  // 0 unknown, 1 ok, 2 not sm_100
+  static std::atomic<int> cached[64];  // 0 unknown, 1 ok, 2 not sm_100
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return ATTN_ERR_DEVICE;
-  if (cached[dev] == 0) {
+  int state = cached[dev].load(std::memory_order_relaxed);
+  if (state == 0) {
     int major = 0, minor = 0;
     if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
         cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess)
       return ATTN_ERR_DEVICE;
-    cached[dev] = (major == 10 && minor == 0) ? 1 : 2;
+    state = (major == 10 && minor == 0) ? 1 : 2;
+    cached[dev].store(state, std::memory_order_relaxed);
   }
-  return cached[dev] == 1 ? ATTN_OK : ATTN_ERR_DEVICE;
+  return state == 1 ? ATTN_OK : ATTN_ERR_DEVICE;
 }
 
 }  // namespace ra
