@@ -25,6 +25,33 @@ inline EncodeTiledFn tensor_map_encoder() {
   return fn;
 }
 
+// The TMA encoder is a driver call and needs a current context on the calling
+// thread.  A host thread that has made no CUDA runtime call yet has none (the
+// runtime binds the device's primary context lazily, on the first call that
+// needs it), so this binds it there: only when no context is current, so a
+// context the caller made current is never replaced.  Returns false if that
+// fails.  Checked once per thread and device.
+inline bool tensor_map_context_ready() {
+  thread_local int ready_dev = -1;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  if (ready_dev == dev) return true;
+  using GetCurrentFn = CUresult (*)(CUcontext*);
+  static GetCurrentFn get_current = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<GetCurrentFn>(nullptr);
+    return reinterpret_cast<GetCurrentFn>(p);
+  }();
+  CUcontext ctx = nullptr;
+  if (!get_current || get_current(&ctx) != CUDA_SUCCESS) return false;
+  if (ctx == nullptr && cudaSetDevice(dev) != cudaSuccess) return false;
+  ready_dev = dev;
+  return true;
+}
+
 // 3-D map over a row-major [outer, rows, inner] tensor of 16-bit elements with
 // the given element strides, loaded/stored in boxes of
 // [1, box_rows, box_inner] with 128-byte swizzle (box_inner * 2 must be 128).
@@ -33,7 +60,7 @@ inline int make_tensor_map_3d(CUtensorMap* map, const void* base, bool bf16, uin
                               uint64_t outer, uint64_t row_stride_elems, uint64_t outer_stride_elems,
                               uint32_t box_inner, uint32_t box_rows) {
   EncodeTiledFn enc = tensor_map_encoder();
-  if (!enc) return -1;
+  if (!enc || !tensor_map_context_ready()) return -1;
   cuuint64_t dims[3] = {inner, rows, outer};
   cuuint64_t strides[2] = {row_stride_elems * 2, outer_stride_elems * 2};
   cuuint32_t box[3] = {box_inner, box_rows, 1};
@@ -61,7 +88,7 @@ inline int make_tensor_map_4d(CUtensorMap* map, const void* base, bool bf16, uin
   for (uint64_t b : sb)
     if (b == 0 || (b & 15u) != 0 || b >= (uint64_t(1) << 40)) return -2;
   EncodeTiledFn enc = tensor_map_encoder();
-  if (!enc) return -1;
+  if (!enc || !tensor_map_context_ready()) return -1;
   cuuint64_t dims[4] = {inner, rows, heads, batch};
   cuuint64_t strides[3] = {sb[0], sb[1], sb[2]};
   cuuint32_t box[4] = {box_inner, box_rows, 1, 1};
