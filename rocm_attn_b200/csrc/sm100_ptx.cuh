@@ -297,12 +297,35 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo_byte
   return d;
 }
 
+// The descriptor of the operand `offset_bytes` (a multiple of 16) past the
+// one `desc` describes: only the 14-bit address field (bits 0-13, address >>
+// 4) changes, and shared-memory addresses (< 256 KB) never carry out of it,
+// so a 32-bit add on the low word is exact.
+__device__ __forceinline__ uint64_t sw128_desc_step(uint64_t desc, uint32_t offset_bytes) {
+  const uint32_t lo = static_cast<uint32_t>(desc) + (offset_bytes >> 4);
+  return (desc & 0xFFFFFFFF00000000ull) | lo;
+}
+
 // Instruction descriptor for kind::f16 with fp32 accumulation.
 //   bits 4-5 D format (1 = f32), 7-9 A format, 10-12 B format (0 f16, 1 bf16),
 //   bit 15 A major, bit 16 B major (0 = K, 1 = MN), 17-22 N>>3, 24-28 M>>4.
 __host__ __device__ constexpr uint32_t umma_idesc_f16(bool bf16, uint32_t M, uint32_t N, bool b_mn_major) {
   return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) | ((b_mn_major ? 1u : 0u) << 16) |
          ((N >> 3) << 17) | ((M >> 4) << 24);
+}
+
+// Per-thread register budget of the executing warp (all warps of a warpgroup
+// execute the same one): dec releases registers to the CTA's pool, inc waits
+// until the pool holds enough.  Counts are multiples of 8 in [24, 256].
+template <int kRegs>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  static_assert(kRegs % 8 == 0 && kRegs >= 24 && kRegs <= 256, "register count");
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegs));
+}
+template <int kRegs>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  static_assert(kRegs % 8 == 0 && kRegs >= 24 && kRegs <= 256, "register count");
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegs));
 }
 
 // ---------------------------------------------------------------------------
