@@ -89,10 +89,6 @@ struct AttnParams {
   int drop_arrival;            // watchdog test build only: lose one P arrival of CTA 0
 };
 
-#ifndef RA_REGSPLIT
-#define RA_REGSPLIT 0
-#endif
-
 // Compile-time shape of the pipeline for head dimension kD, kTiles 128-row
 // Q tiles per CTA and kBlockKeys keys per K/V block.
 template <int kD, int kTiles, int kBlockKeys>
@@ -121,16 +117,7 @@ struct Cfg {
   static constexpr uint32_t kColO = kSepP ? kColP + 64 * kTiles : kBN * kTiles;  // O per tile (kD columns)
   static constexpr int kMmaWarp = 4 * kTiles;            // after the softmax warpgroups
   static constexpr int kTmaWarp = 4 * kTiles + 1;
-  // Two-tile CTAs with a register split: a third, full warpgroup (MMA warp,
-  // TMA warp and two idle warps) gives registers to the softmax warpgroups
-  // with setmaxnreg.  Launched at kRegLaunch per thread (12 warps, one CTA
-  // per SM); warpgroup 2 drops to kRegLow, the softmax rises to kRegHigh.
-  static constexpr bool kRegSplit = RA_REGSPLIT != 0 && kTiles == 2;
-  static constexpr int kThreads = kRegSplit ? 384 : 128 * kTiles + 64;
-  static constexpr int kRegLaunch = 168, kRegLow = 56, kRegHigh = 224;
-  static_assert(!kRegSplit || 256 * (kRegHigh - kRegLaunch) <= 128 * (kRegLaunch - kRegLow),
-                "softmax increase must fit in what warpgroup 2 releases");
-  static_assert(!kRegSplit || 384 * kRegLaunch <= 65536, "launch registers exceed the register file");
+  static constexpr int kThreads = 128 * kTiles + 64;
   static constexpr int kMinBlocksPerSm = kTiles == 2 ? 1 : (kBN == 64 ? 3 : 2);  // one-tile CTAs share an SM
 };
 
@@ -314,18 +301,12 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles, kBlockKeys>::kThreads, Cfg<kD,
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = ctl.tmem_base;
-  // Register split (two-tile CTAs): at the top of each role below, every
-  // warp of warpgroup 2 (MMA, TMA and two idle warps) releases registers and
-  // the softmax warpgroups take them; the increase waits until the release is
-  // done.  Every warp of a warpgroup executes the same setmaxnreg.
-
   RA_MARK(8190 - warp);
   // The last block loaded into each K / V stage (TMA warp; block 0 was issued
   // during setup), for the drain of an aborted CTA.
   int last_k[3] = {0, -1, -1}, last_v[3] = {0, -1, -1};
   if (warp == C::kTmaWarp) {
     // ------------------------------------------------------------------ TMA
-    if constexpr (C::kRegSplit) setmaxnreg_dec<C::kRegLow>();
     const uint64_t pol_keep = l2_policy_evict_last();
     const bool leader = elect_one();
     bool ok = true;
@@ -358,7 +339,6 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles, kBlockKeys>::kThreads, Cfg<kD,
     }
   } else if (warp == C::kMmaWarp) {
     // ------------------------------------------------------------------ UMMA
-    if constexpr (C::kRegSplit) setmaxnreg_dec<C::kRegLow>();
     const uint32_t idesc_s = umma_idesc_f16(kBf16, 128, C::kBN, false);
     const uint32_t idesc_o = umma_idesc_f16(kBf16, 128, kD, true);
     const bool leader = elect_one();
@@ -525,9 +505,8 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles, kBlockKeys>::kThreads, Cfg<kD,
     __syncwarp();
     volatile int no_abort = 0;
     mbar_wait(&ctl.mma_done, 0, &no_abort, status, kWatchDrain + 1);
-  } else if (warp < 4 * kTiles) {
+  } else {
     // --------------------------------------------------------------- softmax
-    if constexpr (C::kRegSplit) setmaxnreg_inc<C::kRegHigh>();
     const int t = warp >> 2;                       // Q tile of this warpgroup
     const int row_in_tile = (warp & 3) * 32 + lane; // == TMEM lane
     const int row_abs = q0 + t * 128 + row_in_tile;
@@ -749,9 +728,6 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles, kBlockKeys>::kThreads, Cfg<kD,
       tma_store_commit();
       tma_store_wait_smem_read();
     }
-  } else {
-    // The idle warps of warpgroup 2 (register split only).
-    if constexpr (C::kRegSplit) setmaxnreg_dec<C::kRegLow>();
   }
 
   RA_MARK(8180 - warp);
@@ -900,13 +876,6 @@ int launch_fwd(const FwdArgs<kMaxProblems>& a, cudaStream_t stream) {
       if (kTiles == 1 && cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
                                               static_cast<int>(cudaSharedmemCarveoutMaxShared)) != cudaSuccess)
         return ATTN_ERR_LAUNCH;
-      if constexpr (C::kRegSplit) {
-        // The register split adds up only for a kernel launched with exactly
-        // kRegLaunch registers per thread; with fewer, the softmax's increase
-        // could never be met.  Refuse to launch such a build.
-        cudaFuncAttributes fa{};
-        if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess || fa.numRegs != C::kRegLaunch) return ATTN_ERR_LAUNCH;
-      }
       configured[dev] = true;
     }
   }

@@ -314,20 +314,6 @@ __host__ __device__ constexpr uint32_t umma_idesc_f16(bool bf16, uint32_t M, uin
          ((N >> 3) << 17) | ((M >> 4) << 24);
 }
 
-// Per-thread register budget of the executing warp (all warps of a warpgroup
-// execute the same one): dec releases registers to the CTA's pool, inc waits
-// until the pool holds enough.  Counts are multiples of 8 in [24, 256].
-template <int kRegs>
-__device__ __forceinline__ void setmaxnreg_inc() {
-  static_assert(kRegs % 8 == 0 && kRegs >= 24 && kRegs <= 256, "register count");
-  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegs));
-}
-template <int kRegs>
-__device__ __forceinline__ void setmaxnreg_dec() {
-  static_assert(kRegs % 8 == 0 && kRegs >= 24 && kRegs <= 256, "register count");
-  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegs));
-}
-
 // ---------------------------------------------------------------------------
 // Numeric helpers
 // ---------------------------------------------------------------------------
