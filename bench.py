@@ -461,6 +461,12 @@ def per_config_table(args, dev, stream, flush, headline: dict):
                         "frac_of_spec_2250": round(tf / SPEC_DENSE_FP16_TFLOPS, 4),
                         "hbm_gbs": round(byts / (ms * 1e-3) / 1e9, 1),
                         "frac_of_measured_hbm": round(byts / (ms * 1e-3) / 1e9 / hbm, 4)})
+            # Roofline of the workload shape by shape: each shape bound by
+            # the slower of its FLOPs at the measured GEMM peak and its bytes
+            # at the measured HBM bandwidth (a mixed list has shapes of both
+            # kinds), summed; the fraction is that time over the measured one.
+            roof_ms = sum(max(s.flops(w.causal) / (burst * 1e12), s.io_bytes() / (hbm * 1e9)) for s in w.shapes) * 1e3
+            row.update({"shape_roofline_ms": round(roof_ms, 4), "frac_of_shape_roofline": round(roof_ms / ms, 4)})
             if len(w.shapes) > 1:
                 # the same sequence as one call of the batch entry point
                 # (grouped tensor-core grids), and both sequences replayed
@@ -484,6 +490,7 @@ def per_config_table(args, dev, stream, flush, headline: dict):
                     gms = statistics.median(time_steps(graph.replay, steps, args.warmup, flush, stream))
                     row[name] = round(gms, 4)
                     del graph
+                row["frac_of_shape_roofline_batch_graph"] = round(roof_ms / row["batch_graph_ms"], 4)
             if reuse and headline.get("parity") is not None:
                 row["parity"] = headline["parity"]
             elif not args.no_parity:
