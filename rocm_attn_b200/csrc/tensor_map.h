@@ -52,26 +52,6 @@ inline bool tensor_map_context_ready() {
   return true;
 }
 
-// 3-D map over a row-major [outer, rows, inner] tensor of 16-bit elements with
-// the given element strides, loaded/stored in boxes of
-// [1, box_rows, box_inner] with 128-byte swizzle (box_inner * 2 must be 128).
-// Returns 0 on success, a CUresult otherwise.
-inline int make_tensor_map_3d(CUtensorMap* map, const void* base, bool bf16, uint64_t inner, uint64_t rows,
-                              uint64_t outer, uint64_t row_stride_elems, uint64_t outer_stride_elems,
-                              uint32_t box_inner, uint32_t box_rows) {
-  EncodeTiledFn enc = tensor_map_encoder();
-  if (!enc || !tensor_map_context_ready()) return -1;
-  cuuint64_t dims[3] = {inner, rows, outer};
-  cuuint64_t strides[2] = {row_stride_elems * 2, outer_stride_elems * 2};
-  cuuint32_t box[3] = {box_inner, box_rows, 1};
-  cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
-                   const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return static_cast<int>(r);
-}
-
 // 4-D map over a [batch, heads, rows, inner] tensor of 16-bit elements whose
 // innermost dimension is contiguous and whose other dimensions have the given
 // element strides (any order in memory, e.g. the [B, L, H, D] layout viewed
