@@ -38,6 +38,7 @@
 
 #include <atomic>
 #include <mutex>
+#include <vector>
 
 namespace ra {
 
@@ -477,30 +478,21 @@ __device__ __forceinline__ uint32_t pack16x2(float lo, float hi) {
   return w;
 }
 
-// kNK: 16-key groups (Skv <= 16 kNK).
+// One (batch, head) slice on one warp: qp, kp, vp point at its first row
+// (row strides q_row, k_row, v_row elements), ob at its contiguous output;
+// sQ, sK, sV are the warp's staging buffers.  kNK: 16-key groups (Skv <= 16 kNK).
 template <bool kBf16, int kD, int kNK>
-__global__ void __launch_bounds__(kMmaWarps * 32) attn_small_mma_kernel(const uint16_t* __restrict__ q,
-                                                                        const uint16_t* __restrict__ k,
-                                                                        const uint16_t* __restrict__ v,
-                                                                        uint16_t* __restrict__ o, bool causal,
-                                                                        int BH, int H, int Sq, int Skv,
-                                                                        float scale_log2, const GeneralStrides st) {
+__device__ __forceinline__ void small_mma_slice(const uint16_t* __restrict__ qp, const uint16_t* __restrict__ kp,
+                                                const uint16_t* __restrict__ vp, uint16_t* __restrict__ ob,
+                                                bool causal, int Sq, int Skv, float scale_log2, long long q_row,
+                                                long long k_row, long long v_row, uint16_t* sQ, uint16_t* sK,
+                                                uint16_t* sV, int lane) {
   constexpr int kRow = kD + 8;        // padded row of a staged matrix, in 16-bit elements
   constexpr int kKeys = 16 * kNK;
   constexpr int kChunks = kD / 8;     // 16-byte chunks per row
-  extern __shared__ __align__(16) unsigned char mma_smem[];
-  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
-  uint16_t* sQ = reinterpret_cast<uint16_t*>(mma_smem) + static_cast<size_t>(warp) * (16 + 2 * kKeys) * kRow;
-  uint16_t* sK = sQ + 16 * kRow;
-  uint16_t* sV = sK + kKeys * kRow;
   const int g = lane >> 2, t4 = lane & 3;  // row within an 8-row group, lane within the row quad
   const int mi = lane >> 3, ri = lane & 7; // ldmatrix: matrix and row this lane addresses
-
-  for (int bh = blockIdx.x * kMmaWarps + warp; bh < BH; bh += gridDim.x * kMmaWarps) {
-    const long long b = bh / H, h = bh - b * H;
-    const uint16_t* qp = q + b * st.q[0] + h * st.q[1];
-    const uint16_t* kp = k + b * st.k[0] + h * st.k[1];
-    const uint16_t* vp = v + b * st.v[0] + h * st.v[1];
+  {
     __syncwarp();  // the previous slice's staging is no longer read
     // Stage Q (16 rows) and K, V (kKeys rows) with 16-byte asynchronous
     // copies, all in flight at once, zero-filled past Sq / Skv.
@@ -512,17 +504,17 @@ __global__ void __launch_bounds__(kMmaWarps * 32) attn_small_mma_kernel(const ui
       bool in;
       if (r < 16) {
         in = r < Sq;
-        src = qp + (in ? r : 0) * st.q[2] + c;
+        src = qp + (in ? r : 0) * q_row + c;
         dst = sQ + r * kRow + c;
       } else if (r < 16 + kKeys) {
         const int key = r - 16;
         in = key < Skv;
-        src = kp + (in ? key : 0) * st.k[2] + c;
+        src = kp + (in ? key : 0) * k_row + c;
         dst = sK + key * kRow + c;
       } else {
         const int key = r - 16 - kKeys;
         in = key < Skv;
-        src = vp + (in ? key : 0) * st.v[2] + c;
+        src = vp + (in ? key : 0) * v_row + c;
         dst = sV + key * kRow + c;
       }
       cp_async16(static_cast<uint32_t>(__cvta_generic_to_shared(dst)), src, in);
@@ -604,7 +596,6 @@ __global__ void __launch_bounds__(kMmaWarps * 32) attn_small_mma_kernel(const ui
       }
     }
     const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f, inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
-    uint16_t* ob = o + static_cast<size_t>(bh) * Sq * kD;
 #pragma unroll
     for (int n = 0; n < kD / 8; ++n) {
       const int col = 8 * n + 2 * t4;
@@ -612,6 +603,69 @@ __global__ void __launch_bounds__(kMmaWarps * 32) attn_small_mma_kernel(const ui
       if (g + 8 < Sq)
         *reinterpret_cast<uint32_t*>(ob + (g + 8) * kD + col) = pack16x2<kBf16>(of[n][2] * inv1, of[n][3] * inv1);
     }
+  }
+}
+
+// The warp's staging buffers in dynamic shared memory.
+template <int kD, int kNK>
+__device__ __forceinline__ uint16_t* small_mma_staging(unsigned char* smem, int warp) {
+  return reinterpret_cast<uint16_t*>(smem) + static_cast<size_t>(warp) * (16 + 2 * 16 * kNK) * (kD + 8);
+}
+
+template <bool kBf16, int kD, int kNK>
+__global__ void __launch_bounds__(kMmaWarps * 32) attn_small_mma_kernel(const uint16_t* __restrict__ q,
+                                                                        const uint16_t* __restrict__ k,
+                                                                        const uint16_t* __restrict__ v,
+                                                                        uint16_t* __restrict__ o, bool causal,
+                                                                        int BH, int H, int Sq, int Skv,
+                                                                        float scale_log2, const GeneralStrides st) {
+  extern __shared__ __align__(16) unsigned char mma_smem[];
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  uint16_t* sQ = small_mma_staging<kD, kNK>(mma_smem, warp);
+  uint16_t* sK = sQ + 16 * (kD + 8);
+  uint16_t* sV = sK + 16 * kNK * (kD + 8);
+  for (int bh = blockIdx.x * kMmaWarps + warp; bh < BH; bh += gridDim.x * kMmaWarps) {
+    const long long b = bh / H, h = bh - b * H;
+    small_mma_slice<kBf16, kD, kNK>(q + b * st.q[0] + h * st.q[1], k + b * st.k[0] + h * st.k[1],
+                                    v + b * st.v[0] + h * st.v[1], o + static_cast<size_t>(bh) * Sq * kD, causal,
+                                    Sq, Skv, scale_log2, st.q[2], st.k[2], st.v[2], sQ, sK, sV, lane);
+  }
+}
+
+// Several problems of one dtype, head dim and key-group count in one grid:
+// slot i holds problem i and the running total of slices up to and
+// including it; warps walk the global slice index and find its problem.
+struct SmallSlot {
+  const uint16_t *q, *k, *v;
+  uint16_t* o;
+  GeneralStrides st;
+  long long slice_end;
+  int H, Sq, Skv, causal;
+  float scale_log2;
+};
+struct SmallGroupArgs {
+  SmallSlot p[kSmallGroupMax];
+  int n;
+};
+
+template <bool kBf16, int kD, int kNK>
+__global__ void __launch_bounds__(kMmaWarps * 32) attn_small_mma_group_kernel(const __grid_constant__ SmallGroupArgs a) {
+  extern __shared__ __align__(16) unsigned char mma_smem[];
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  uint16_t* sQ = small_mma_staging<kD, kNK>(mma_smem, warp);
+  uint16_t* sK = sQ + 16 * (kD + 8);
+  uint16_t* sV = sK + 16 * kNK * (kD + 8);
+  const long long total = a.p[a.n - 1].slice_end;
+  int pi = 0;  // a warp's slices only increase, so its problem index only moves forward
+  for (long long s = static_cast<long long>(blockIdx.x) * kMmaWarps + warp; s < total;
+       s += static_cast<long long>(gridDim.x) * kMmaWarps) {
+    while (s >= a.p[pi].slice_end) ++pi;
+    const SmallSlot& P = a.p[pi];
+    const long long bh = s - (pi > 0 ? a.p[pi - 1].slice_end : 0);
+    const long long b = bh / P.H, h = bh - b * P.H;
+    small_mma_slice<kBf16, kD, kNK>(P.q + b * P.st.q[0] + h * P.st.q[1], P.k + b * P.st.k[0] + h * P.st.k[1],
+                                    P.v + b * P.st.v[0] + h * P.st.v[1], P.o + bh * P.Sq * kD, P.causal != 0, P.Sq,
+                                    P.Skv, P.scale_log2, P.st.q[2], P.st.k[2], P.st.v[2], sQ, sK, sV, lane);
   }
 }
 
@@ -630,6 +684,38 @@ int launch_small_mma_typed(const void* q, const void* k, const void* v, void* ou
                                                static_cast<const uint16_t*>(v), static_cast<uint16_t*>(out), causal,
                                                BH, H, Sq, Skv, scale_log2, st);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+template <bool kBf16, int kD, int kNK>
+int launch_small_mma_group_typed(const SmallGroupArgs& a, cudaStream_t stream) {
+  constexpr int smem = kMmaWarps * (16 + 2 * 16 * kNK) * (kD + 8) * 2;
+  auto kern = attn_small_mma_group_kernel<kBf16, kD, kNK>;
+  static SmemOptIn opt_in;
+  const int sms = current_sm_count();
+  if (sms == 0 || !opt_in.ensure(kern, smem)) return -1;
+  const long long need = (a.p[a.n - 1].slice_end + kMmaWarps - 1) / kMmaWarps;
+  const unsigned grid = static_cast<unsigned>(need < 32LL * sms ? need : 32LL * sms);
+  kern<<<grid, kMmaWarps * 32, smem, stream>>>(a);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+template <bool kBf16, int kD>
+int launch_small_mma_group_d(const SmallGroupArgs& a, int nk, cudaStream_t stream) {
+  switch (nk) {
+    case 1: return launch_small_mma_group_typed<kBf16, kD, 1>(a, stream);
+    case 2: return launch_small_mma_group_typed<kBf16, kD, 2>(a, stream);
+    default: return launch_small_mma_group_typed<kBf16, kD, 4>(a, stream);
+  }
+}
+
+template <bool kBf16>
+int launch_small_mma_group(const SmallGroupArgs& a, int D, int nk, cudaStream_t stream) {
+  switch (D) {
+    case 16: return launch_small_mma_group_d<kBf16, 16>(a, nk, stream);
+    case 32: return launch_small_mma_group_d<kBf16, 32>(a, nk, stream);
+    case 64: return launch_small_mma_group_d<kBf16, 64>(a, nk, stream);
+    default: return launch_small_mma_group_d<kBf16, 128>(a, nk, stream);
+  }
 }
 
 template <bool kBf16, int kD>
@@ -911,6 +997,49 @@ int launch_attn_small(const void* q, const void* k, const void* v, void* out, in
     case 64: return launch_small_keys<64>(q, k, v, out, dtype, causal, bh, H, Sq, Skv, sl, st, stream);
     default: return launch_small_keys<128>(q, k, v, out, dtype, causal, bh, H, Sq, Skv, sl, st, stream);
   }
+}
+
+int small_mma_group_key(int Sq, int Skv, int D, int dtype) {
+  if (dtype == 2 || Sq > 16 || !small_kernel_takes(Sq, Skv, D, dtype)) return 0;
+  return Skv <= 16 ? 1 : Skv <= 32 ? 2 : 4;
+}
+
+int launch_attn_small_grouped(const SmallProblem* p, int n, int D, int dtype, cudaStream_t stream,
+                              std::vector<int>* fallback) {
+  if (n <= 0) return 0;
+  const int nk = small_mma_group_key(p[0].Sq, p[0].Skv, D, dtype);
+  if (nk == 0) return -1;
+  SmallGroupArgs a{};
+  auto flush = [&]() -> int {
+    if (a.n == 0) return 0;
+    const int r = dtype == 1 ? launch_small_mma_group<true>(a, D, nk, stream)
+                             : launch_small_mma_group<false>(a, D, nk, stream);
+    a.n = 0;
+    return r;
+  };
+  auto a16 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; };
+  long long slices = 0;
+  for (int i = 0; i < n; ++i) {
+    const SmallProblem& q = p[i];
+    const long long BH = static_cast<long long>(q.B) * q.H;
+    bool rows16 = a16(q.q) && a16(q.k) && a16(q.v) && a16(q.out);
+    for (const long long* s3 : {q.st.q, q.st.k, q.st.v})
+      for (int j = 0; j < 3; ++j) rows16 = rows16 && (s3[j] * 2) % 16 == 0;
+    if (small_mma_group_key(q.Sq, q.Skv, D, dtype) != nk || BH <= 0 || BH > 0x7fffffffLL || !rows16) {
+      fallback->push_back(i);  // the caller runs it alone
+      continue;
+    }
+    if (a.n == kSmallGroupMax) {
+      if (flush() != 0) return -1;
+      slices = 0;
+    }
+    slices += BH;
+    a.p[a.n] = SmallSlot{static_cast<const uint16_t*>(q.q), static_cast<const uint16_t*>(q.k),
+                         static_cast<const uint16_t*>(q.v), static_cast<uint16_t*>(q.out), q.st, slices, q.H, q.Sq,
+                         q.Skv, q.causal ? 1 : 0, q.scale * 1.4426950408889634f};
+    ++a.n;
+  }
+  return flush();
 }
 
 int launch_attn_general(const void* q, const void* k, const void* v, void* out, int B, int H, int Sq, int Skv,

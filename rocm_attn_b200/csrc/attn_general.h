@@ -4,6 +4,8 @@
 
 #include <cuda_runtime.h>
 
+#include <vector>
+
 namespace ra {
 
 // Largest head dimension the general kernel takes.
@@ -39,6 +41,29 @@ bool small_kernel_takes(int Sq, int Skv, int D, int dtype);
 // (nothing launched) when they do not.
 int launch_attn_small(const void* q, const void* k, const void* v, void* out, int B, int H, int Sq, int Skv, int D,
                       bool causal, float scale, int dtype, const GeneralStrides& strides, cudaStream_t stream);
+
+// Grouped launches of the warp-level tensor-core short kernel (fp16/bf16,
+// Sq <= 16): problems with the same dtype, head dim and 16-key group count
+// (small_mma_group_key) run in one grid, up to kSmallGroupMax per grid, each
+// slice computed exactly as a single launch computes it.
+constexpr int kSmallGroupMax = 16;
+struct SmallProblem {
+  const void *q, *k, *v;
+  void* out;
+  int B, H, Sq, Skv;
+  bool causal;
+  float scale;
+  GeneralStrides st;
+};
+// The group key of a problem: its 16-key group count (1, 2 or 4), or 0 when
+// it does not take the warp-level tensor-core short kernel.
+int small_mma_group_key(int Sq, int Skv, int D, int dtype);
+// Launches the n problems (all of head dim D, dtype 0 or 1 and one group
+// key) as few grids as kSmallGroupMax allows.  Problems whose rows are not
+// 16-byte aligned are not launched; their indices go to *fallback.  Returns
+// 0, or -1 if a grid could not be launched.
+int launch_attn_small_grouped(const SmallProblem* p, int n, int D, int dtype, cudaStream_t stream,
+                              std::vector<int>* fallback);
 
 // Mid-length sequences on warp-level tensor cores (fp16/bf16, 16-byte aligned
 // rows): every D = 16 / 32 problem, and D = 64 with Sq <= kMidMaxQueries and

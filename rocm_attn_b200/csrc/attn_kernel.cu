@@ -263,11 +263,37 @@ extern "C" int launch_attn_forward_batch(const AttnProblem* problems, int n, Att
     if (st != ATTN_OK) return st;
   }
   // Problems of the tensor-core route that share an instantiation run as one
-  // grid (launch_tc_grouped); the others launch one by one.
+  // grid (launch_tc_grouped), and so do short problems of the warp-level
+  // tensor-core kernel with the same head dim and key-group count
+  // (launch_attn_small_grouped); the others launch one by one.
+  const int dt = static_cast<int>(dtype);
   std::vector<bool> done(static_cast<size_t>(n), false);
   for (int i = 0; i < n; ++i) {
     if (done[static_cast<size_t>(i)]) continue;
     const Call& c = calls[static_cast<size_t>(i)];
+    const int nk = c.route == Route::kSmall ? small_mma_group_key(c.prob.Sq, c.prob.Skv, c.D, dt) : 0;
+    if (nk > 0) {
+      std::vector<SmallProblem> group;
+      std::vector<int> members;
+      for (int j = i; j < n; ++j) {
+        const Call& o = calls[static_cast<size_t>(j)];
+        if (!done[static_cast<size_t>(j)] && o.route == Route::kSmall && o.D == c.D &&
+            small_mma_group_key(o.prob.Sq, o.prob.Skv, o.D, dt) == nk) {
+          const FwdProblem& d = o.prob;
+          group.push_back(SmallProblem{d.q, d.k, d.v, d.out, d.B, d.H, d.Sq, d.Skv, o.causal, d.scale, o.gs});
+          members.push_back(j);
+          done[static_cast<size_t>(j)] = true;
+        }
+      }
+      std::vector<int> fallback;
+      if (launch_attn_small_grouped(group.data(), static_cast<int>(group.size()), c.D, dt, stream, &fallback) != 0)
+        return ATTN_ERR_LAUNCH;
+      for (int f : fallback) {  // rows not 16-byte aligned: the single-call route and its fallbacks
+        const int g = run(calls[static_cast<size_t>(members[static_cast<size_t>(f)])], stream);
+        if (g != ATTN_OK) return g;
+      }
+      continue;
+    }
     if (c.route != Route::kTensorCore) {
       const int st = run(c, stream);
       if (st != ATTN_OK) return st;

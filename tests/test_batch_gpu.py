@@ -132,3 +132,52 @@ def test_batch_through_the_c_abi(attn):
     bad[1] = AttnProblem(ins[1][0].data_ptr(), ins[1][1].data_ptr(), ins[1][2].data_ptr(), outs[1].data_ptr(),
                          1, 8, 256, 900, 1000, False, -1.0, None, None, None)
     assert lib.launch_attn_forward_batch(bad, 2, 0, None) == 2  # ATTN_ERR_UNSUPPORTED
+
+
+def test_short_problems_grouped_through_the_c_abi(attn):
+    # 21 short problems (<= 16 queries) for the warp-level tensor-core kernel,
+    # each with its own causal flag: 17 of one head dim and key-group count
+    # (two grids, 16 + 1), three with 17-32 keys (another group), and one
+    # whose K rows are 136 bytes apart, which the grouped kernel cannot stage
+    # with 16-byte copies: it runs alone (general kernel).  Every output must
+    # equal its own strided single call bit for bit, and meet the oracle.
+    lib = ctypes.CDLL(attn.KERNEL_LIB_PATH)
+    lib.launch_attn_forward_batch.argtypes = [ctypes.POINTER(AttnProblem), ctypes.c_int, ctypes.c_int,
+                                              ctypes.c_void_p]
+    lib.launch_attn_forward_batch.restype = ctypes.c_int
+    lib.launch_attn_forward_strided.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int] * 5 + [
+        ctypes.c_bool, ctypes.c_float, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+        ctypes.c_void_p]
+    lib.launch_attn_forward_strided.restype = ctypes.c_int
+    shapes = [Shape(1 + i % 5, 1 + i % 3, 1 + i % 16, 1 + (5 * i) % 16, 64) for i in range(17)]
+    shapes += [Shape(3, 2, 16, 17 + 5 * i, 64) for i in range(3)]
+    shapes += [Shape(2, 3, 12, 16, 64)]
+    causal = [i % 2 == 1 for i in range(len(shapes))]
+    ins = _inputs(shapes, torch.float16, 21)
+    # the last problem's K: rows of 68 elements in storage, 64 used
+    s = shapes[-1]
+    kpad = torch.zeros(s.B, s.H, s.Lk, 68, device="cuda", dtype=torch.float16)
+    kpad[..., :64] = ins[-1][1]
+    ins[-1] = (ins[-1][0], kpad[..., :64], ins[-1][2])
+    strides = []
+    for q, k, v in ins:
+        strides.append(tuple((ctypes.c_longlong * 3)(*t.stride()[:3]) for t in (q, k, v)))
+    outs = [torch.empty_like(t[0]) for t in ins]
+    arr = (AttnProblem * len(shapes))()
+    for i, (sh, (q, k, v), o, st) in enumerate(zip(shapes, ins, outs, strides)):
+        arr[i] = AttnProblem(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), sh.B, sh.H, sh.Lq, sh.Lk, sh.D,
+                             causal[i], -1.0, ctypes.addressof(st[0]), ctypes.addressof(st[1]),
+                             ctypes.addressof(st[2]))
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    assert lib.launch_attn_forward_batch(arr, len(shapes), 0, stream) == 0
+    singles = [torch.empty_like(t[0]) for t in ins]
+    for i, (sh, (q, k, v), r, st) in enumerate(zip(shapes, ins, singles, strides)):
+        assert lib.launch_attn_forward_strided(q.data_ptr(), k.data_ptr(), v.data_ptr(), r.data_ptr(), sh.B, sh.H,
+                                               sh.Lq, sh.Lk, sh.D, causal[i], -1.0, 0, ctypes.addressof(st[0]),
+                                               ctypes.addressof(st[1]), ctypes.addressof(st[2]), stream) == 0
+    torch.cuda.synchronize()
+    for i, (sh, o, r) in enumerate(zip(shapes, outs, singles)):
+        assert torch.equal(o, r), f"problem {i} {sh} causal={causal[i]}: batched output differs from the single call"
+    for i, (sh, (q, k, v), o) in enumerate(zip(shapes, ins, outs)):
+        _check_oracle(sh, q, k.contiguous(), v, o, torch.float16, causal[i])
+    assert attn.check_status(0) == 0
