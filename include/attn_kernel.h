@@ -111,7 +111,10 @@ typedef struct AttnProblem {
  * dim, masking and tile shape share one grid (up to 16 problems per grid),
  * whose work units are ordered longest first, so the short units of one
  * problem fill the last wave of another and no launch waits for the tail of
- * the previous one.  The others are launched one by one.  Every problem is
+ * the previous one.  Short problems (fp16/bf16, at most 16 queries and 64
+ * keys) with the same head dim and 16-key group count share one grid of the
+ * warp-level tensor-core kernel the same way.  The others are launched one
+ * by one.  Every problem is
  * checked before anything is launched; on an error nothing was launched.
  * The output buffers must not overlap any input or each other.  No
  * counterpart in the reference, whose benchmark launches one shape at a time
