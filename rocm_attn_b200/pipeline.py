@@ -59,6 +59,29 @@ def _device_state(device: torch.device, key: tuple, q_shape, k_shape, dtype):
         return st
 
 
+def _chunk_sizes(BH: int, base: int, uniform: bool) -> list:
+    """Slices per chunk.  The step ends with the last chunk's attention and
+    device-to-host copy after the last host-to-device copy, so long splits end
+    in chunks that halve down to one slice (2*base, base, ..., 1, 1), and the
+    bulk before them goes in chunks of 3*base: C4 (64 heads, base 4) runs as
+    12,12,12,12,8,4,2,1,1 heads, measured 3 % faster end to end than sixteen
+    chunks of 4.  Short splits (fewer than eight chunks), and an explicit
+    chunk size, stay uniform."""
+    if uniform or BH < 8 * base:
+        return [min(base, BH - c0) for c0 in range(0, BH, base)]
+    tail = []
+    s = 2 * base
+    while s >= 1:
+        tail.append(s)
+        s //= 2
+    tail.append(1)
+    bulk = BH - sum(tail)
+    if bulk <= 0:
+        return [min(base, BH - c0) for c0 in range(0, BH, base)]
+    big = 3 * base
+    return [big] * (bulk // big) + ([bulk % big] if bulk % big else []) + tail
+
+
 def attn_forward_pinned(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = False,
                         scale: Optional[float] = None, out: Optional[torch.Tensor] = None,
                         chunk_slices: Optional[int] = None, device: Optional[torch.device] = None) -> torch.Tensor:
@@ -66,9 +89,10 @@ def attn_forward_pinned(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causa
     k/v [B, H, Lk, D].  Returns O [B, H, Lq, D] in pinned host memory (``out``
     if given).  Asynchronous like the op itself: the result is ready once the
     caller's current stream on ``device`` is synchronised.  ``chunk_slices``
-    (batch, head) slices go per chunk (default: one chunk per about 20 MB of
-    q/k/v, between 2 and 16 chunks; measured best or within 3 % of best from
-    33 MB to 805 MB of inputs, where every chunk adds some host work)."""
+    (batch, head) slices go per chunk (default: a base of one chunk per about
+    20 MB of q/k/v, between 2 and 16 chunks, measured best or within 3 % of
+    best from 33 MB to 805 MB of inputs, where every chunk adds some host work;
+    splits of eight or more chunks end in halving chunks, _chunk_sizes)."""
     from . import attn_forward
 
     for t in (q, k, v) + ((out,) if out is not None else ()):
@@ -93,8 +117,12 @@ def attn_forward_pinned(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causa
         in_bytes = (q.numel() + k.numel() + v.numel()) * q.element_size()
         n_chunks = min(16, max(2, round(in_bytes / 20e6)))
         n = max(1, math.ceil(BH / n_chunks))
-    chunks = [(c0, min(BH, c0 + n)) for c0 in range(0, BH, n)]
-    key = (device, tuple(q.shape), tuple(k.shape), q.dtype, n)
+    sizes = _chunk_sizes(BH, n, uniform=bool(chunk_slices))
+    chunks, c0 = [], 0
+    for sz in sizes:
+        chunks.append((c0, c0 + sz))
+        c0 += sz
+    key = (device, tuple(q.shape), tuple(k.shape), q.dtype, tuple(sizes))
     st = _device_state(device, key, (BH, Lq, D), (BH, Lk, D), q.dtype)
     hq, hk, hv, ho = (t.view(BH, -1, D) for t in (q, k, v, out))
     compute = torch.cuda.current_stream(device)

@@ -65,3 +65,18 @@ def test_pinned_entry_rejects_pageable_tensors():
     x = torch.zeros(1, 1, 8, 64, dtype=torch.float16)
     with pytest.raises(ValueError, match="pinned"):
         rocm_attn_b200.attn_forward_pinned(x, x, x)
+
+
+@pytest.mark.parametrize("BH,base", [(64, 4), (32, 2), (64, 8), (8, 4), (20, 2), (100, 7), (33, 3), (15, 1), (1, 1),
+                                     (5, 16)])
+def test_pinned_chunk_schedule_covers_every_slice(BH, base):
+    from rocm_attn_b200.pipeline import _chunk_sizes
+    sizes = _chunk_sizes(BH, base, uniform=False)
+    assert sum(sizes) == BH and all(s > 0 for s in sizes)
+    if BH >= 8 * base:  # long splits end in chunks that halve down to one slice
+        tail = sizes[-(len(bin(2 * base)) - 2) - 1:]  # 2*base, halvings down to 1, and 1
+        assert tail[0] == 2 * base and tail[-2:] == [1, 1] and tail == sorted(tail, reverse=True)
+    else:
+        assert sizes == [min(base, BH - c) for c in range(0, BH, base)]
+    assert _chunk_sizes(BH, base, uniform=True) == [min(base, BH - c) for c in range(0, BH, base)]
+    assert _chunk_sizes(64, 4, uniform=False) == [12, 12, 12, 12, 8, 4, 2, 1, 1]
