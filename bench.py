@@ -86,6 +86,7 @@ DTYPES, WORKLOADS, Shape, Workload = W.DTYPES, W.WORKLOADS, W.Shape, W.Workload
 METRIC = "attention fwd ms/iter and TFLOPS (% of B200 fp16 TC peak) at 1/2/4/8 GPUs"
 SPEC_DENSE_FP16_TFLOPS = 2250.0
 FALLBACK_HBM_GBS = 6650.0  # earlier measurement on this pool, used without MEASURED_PEAKS.json
+MAX_SM_CLOCK_HZ = 1.965e9  # B200 clocks.max.sm, the clock the MUFU fraction is quoted at
 FALLBACK_PEAK_TFLOPS = 1590.0
 L2_FLUSH_BYTES = 256 << 20
 L2_NOTE = "a 256 MiB buffer rewritten between timed steps, outside the timed region"
@@ -467,6 +468,15 @@ def per_config_table(args, dev, stream, flush, headline: dict):
             # kinds), summed; the fraction is that time over the measured one.
             roof_ms = sum(max(s.flops(w.causal) / (burst * 1e12), s.io_bytes() / (hbm * 1e9)) for s in w.shapes) * 1e3
             row.update({"shape_roofline_ms": round(roof_ms, 4), "frac_of_shape_roofline": round(roof_ms / ms, 4)})
+            # Softmax exponentials (one per unmasked score) and, for the
+            # tensor-core kernel's share on the MUFU (three quarters; the rest
+            # is a polynomial on the FMA pipes), the fraction of the MUFU's
+            # 16 ex2 per clock per SM at the maximum SM clock: D=64 is bound
+            # by them.
+            exps = sum(s.bh * s.unmasked_pairs(w.causal) for s in w.shapes)
+            mufu_peak = 16.0 * torch.cuda.get_device_properties(dev).multi_processor_count * MAX_SM_CLOCK_HZ
+            row.update({"exp_count": exps, "exp_per_s": round(exps / (ms * 1e-3), 1),
+                        "mufu_frac_at_max_clock": round(0.75 * exps / (ms * 1e-3) / mufu_peak, 4)})
             if len(w.shapes) > 1:
                 # the same sequence as one call of the batch entry point
                 # (grouped tensor-core grids), and both sequences replayed
