@@ -302,6 +302,7 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles, kBlockKeys>::kThreads, Cfg<kD,
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = ctl.tmem_base;
+
   RA_MARK(8190 - warp);
   // The last block loaded into each K / V stage (TMA warp; block 0 was issued
   // during setup), for the drain of an aborted CTA.
@@ -700,7 +701,7 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles, kBlockKeys>::kThreads, Cfg<kD,
     // D=64).  The others hand it to the TMA engine, which stores it while the
     // SM keeps working: a copy by the warps measured 1-3 % slower for both
     // tiles of two-tile CTAs and with three 64-key-block CTAs per SM.
-    constexpr bool coop_copy = kTiles == 1 && kBN == 128;
+    constexpr bool kCoopCopy = kTiles == 1 && kBN == 128;
     if (store) {
       tc_fence_after();
       const float inv_l = 1.f / l;
@@ -726,17 +727,17 @@ __global__ void __launch_bounds__(Cfg<kD, kTiles, kBlockKeys>::kThreads, Cfg<kD,
           *reinterpret_cast<uint4*>(stage + off) = v;
         }
       }
-      if constexpr (!coop_copy) fence_proxy_async_smem();
+      if constexpr (!kCoopCopy) fence_proxy_async_smem();
     }
     // All four warps of the group pass this barrier exactly once.
     named_barrier_sync(1 + t, 128);
-    if (store && !coop_copy && (threadIdx.x & 127) == 0) {
+    if (store && !kCoopCopy && (threadIdx.x & 127) == 0) {
       for (int cb = 0; cb < kD / 64; ++cb)
         tma_store_4d(map_o, smem_addr(stage + cb * C::kBlockBytes), cb * 64, q0 + t * 128, hh, bb);
       tma_store_commit();
       tma_store_wait_smem_read();
     }
-    if (store && coop_copy) {
+    if (store && kCoopCopy) {
       // The group copies the staged tile to O (contiguous [B, H, Lq, D]) in
       // 16-byte chunks taken in row-major order, so each warp instruction
       // writes whole rows, 512 contiguous bytes; rows past Lq are skipped.
