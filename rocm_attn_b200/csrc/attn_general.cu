@@ -492,117 +492,115 @@ __device__ __forceinline__ void small_mma_slice(const uint16_t* __restrict__ qp,
   constexpr int kChunks = kD / 8;     // 16-byte chunks per row
   const int g = lane >> 2, t4 = lane & 3;  // row within an 8-row group, lane within the row quad
   const int mi = lane >> 3, ri = lane & 7; // ldmatrix: matrix and row this lane addresses
-  {
-    __syncwarp();  // the previous slice's staging is no longer read
-    // Stage Q (16 rows) and K, V (kKeys rows) with 16-byte asynchronous
-    // copies, all in flight at once, zero-filled past Sq / Skv.
+  __syncwarp();  // the previous slice's staging is no longer read
+  // Stage Q (16 rows) and K, V (kKeys rows) with 16-byte asynchronous
+  // copies, all in flight at once, zero-filled past Sq / Skv.
 #pragma unroll
-    for (int e = lane; e < (16 + 2 * kKeys) * kChunks; e += 32) {
-      const int r = e / kChunks, c = (e - r * kChunks) * 8;
-      const uint16_t* src;
-      uint16_t* dst;
-      bool in;
-      if (r < 16) {
-        in = r < Sq;
-        src = qp + (in ? r : 0) * q_row + c;
-        dst = sQ + r * kRow + c;
-      } else if (r < 16 + kKeys) {
-        const int key = r - 16;
-        in = key < Skv;
-        src = kp + (in ? key : 0) * k_row + c;
-        dst = sK + key * kRow + c;
-      } else {
-        const int key = r - 16 - kKeys;
-        in = key < Skv;
-        src = vp + (in ? key : 0) * v_row + c;
-        dst = sV + key * kRow + c;
-      }
-      cp_async16(static_cast<uint32_t>(__cvta_generic_to_shared(dst)), src, in);
+  for (int e = lane; e < (16 + 2 * kKeys) * kChunks; e += 32) {
+    const int r = e / kChunks, c = (e - r * kChunks) * 8;
+    const uint16_t* src;
+    uint16_t* dst;
+    bool in;
+    if (r < 16) {
+      in = r < Sq;
+      src = qp + (in ? r : 0) * q_row + c;
+      dst = sQ + r * kRow + c;
+    } else if (r < 16 + kKeys) {
+      const int key = r - 16;
+      in = key < Skv;
+      src = kp + (in ? key : 0) * k_row + c;
+      dst = sK + key * kRow + c;
+    } else {
+      const int key = r - 16 - kKeys;
+      in = key < Skv;
+      src = vp + (in ? key : 0) * v_row + c;
+      dst = sV + key * kRow + c;
     }
-    cp_async_commit();
-    cp_async_wait<0>();
-    __syncwarp();
+    cp_async16(static_cast<uint32_t>(__cvta_generic_to_shared(dst)), src, in);
+  }
+  cp_async_commit();
+  cp_async_wait<0>();
+  __syncwarp();
 
-    // S = Q K^T: 2 * kNK n8 tiles of keys, kD / 16 k-steps over the head dim.
-    float sf[2 * kNK][4];
+  // S = Q K^T: 2 * kNK n8 tiles of keys, kD / 16 k-steps over the head dim.
+  float sf[2 * kNK][4];
 #pragma unroll
-    for (int n = 0; n < 2 * kNK; ++n) sf[n][0] = sf[n][1] = sf[n][2] = sf[n][3] = 0.f;
-    const uint32_t q_base = static_cast<uint32_t>(__cvta_generic_to_shared(sQ));
-    const uint32_t k_base = static_cast<uint32_t>(__cvta_generic_to_shared(sK));
-    const uint32_t v_base = static_cast<uint32_t>(__cvta_generic_to_shared(sV));
+  for (int n = 0; n < 2 * kNK; ++n) sf[n][0] = sf[n][1] = sf[n][2] = sf[n][3] = 0.f;
+  const uint32_t q_base = static_cast<uint32_t>(__cvta_generic_to_shared(sQ));
+  const uint32_t k_base = static_cast<uint32_t>(__cvta_generic_to_shared(sK));
+  const uint32_t v_base = static_cast<uint32_t>(__cvta_generic_to_shared(sV));
 #pragma unroll
-    for (int ks = 0; ks < kD / 16; ++ks) {
-      uint32_t a[4];
-      ldsm_x4(q_base + 2 * (((mi & 1) * 8 + ri) * kRow + ks * 16 + (mi >> 1) * 8), a);
+  for (int ks = 0; ks < kD / 16; ++ks) {
+    uint32_t a[4];
+    ldsm_x4(q_base + 2 * (((mi & 1) * 8 + ri) * kRow + ks * 16 + (mi >> 1) * 8), a);
 #pragma unroll
-      for (int nk = 0; nk < kNK; ++nk) {
-        uint32_t bk[4];
-        ldsm_x4(k_base + 2 * ((nk * 16 + (mi >> 1) * 8 + ri) * kRow + ks * 16 + (mi & 1) * 8), bk);
-        mma16816<kBf16>(sf[2 * nk], a, bk[0], bk[1]);
-        mma16816<kBf16>(sf[2 * nk + 1], a, bk[2], bk[3]);
-      }
+    for (int nk = 0; nk < kNK; ++nk) {
+      uint32_t bk[4];
+      ldsm_x4(k_base + 2 * ((nk * 16 + (mi >> 1) * 8 + ri) * kRow + ks * 16 + (mi & 1) * 8), bk);
+      mma16816<kBf16>(sf[2 * nk], a, bk[0], bk[1]);
+      mma16816<kBf16>(sf[2 * nk + 1], a, bk[2], bk[3]);
     }
+  }
 
-    // Softmax over each row (rows g and g + 8 of this lane; its keys are
-    // 8 n + 2 t4 and + 1 of every tile n).
-    float m0 = -INFINITY, m1 = -INFINITY;
+  // Softmax over each row (rows g and g + 8 of this lane; its keys are
+  // 8 n + 2 t4 and + 1 of every tile n).
+  float m0 = -INFINITY, m1 = -INFINITY;
 #pragma unroll
-    for (int n = 0; n < 2 * kNK; ++n) {
+  for (int n = 0; n < 2 * kNK; ++n) {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int key = 8 * n + 2 * t4 + (e & 1);
-        const int row = g + (e >> 1) * 8;
-        const bool masked = key >= Skv || (causal && key > row);
-        sf[n][e] = masked ? -INFINITY : sf[n][e] * scale_log2;
-      }
-      m0 = fmaxf(m0, fmaxf(sf[n][0], sf[n][1]));
-      m1 = fmaxf(m1, fmaxf(sf[n][2], sf[n][3]));
+    for (int e = 0; e < 4; ++e) {
+      const int key = 8 * n + 2 * t4 + (e & 1);
+      const int row = g + (e >> 1) * 8;
+      const bool masked = key >= Skv || (causal && key > row);
+      sf[n][e] = masked ? -INFINITY : sf[n][e] * scale_log2;
     }
-    m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, 1));
-    m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, 2));
-    m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, 1));
-    m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, 2));
-    float l0 = 0.f, l1 = 0.f;
+    m0 = fmaxf(m0, fmaxf(sf[n][0], sf[n][1]));
+    m1 = fmaxf(m1, fmaxf(sf[n][2], sf[n][3]));
+  }
+  m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, 1));
+  m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, 2));
+  m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, 1));
+  m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, 2));
+  float l0 = 0.f, l1 = 0.f;
 #pragma unroll
-    for (int n = 0; n < 2 * kNK; ++n) {
-      sf[n][0] = exp2f(sf[n][0] - m0);
-      sf[n][1] = exp2f(sf[n][1] - m0);
-      sf[n][2] = exp2f(sf[n][2] - m1);
-      sf[n][3] = exp2f(sf[n][3] - m1);
-      l0 += sf[n][0] + sf[n][1];
-      l1 += sf[n][2] + sf[n][3];
-    }
-    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
-    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
-    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
-    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+  for (int n = 0; n < 2 * kNK; ++n) {
+    sf[n][0] = exp2f(sf[n][0] - m0);
+    sf[n][1] = exp2f(sf[n][1] - m0);
+    sf[n][2] = exp2f(sf[n][2] - m1);
+    sf[n][3] = exp2f(sf[n][3] - m1);
+    l0 += sf[n][0] + sf[n][1];
+    l1 += sf[n][2] + sf[n][3];
+  }
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
 
-    // O = P V: P's accumulator fragments are A fragments after packing.
-    float of[kD / 8][4];
+  // O = P V: P's accumulator fragments are A fragments after packing.
+  float of[kD / 8][4];
 #pragma unroll
-    for (int n = 0; n < kD / 8; ++n) of[n][0] = of[n][1] = of[n][2] = of[n][3] = 0.f;
+  for (int n = 0; n < kD / 8; ++n) of[n][0] = of[n][1] = of[n][2] = of[n][3] = 0.f;
 #pragma unroll
-    for (int kk = 0; kk < kNK; ++kk) {
-      const uint32_t a[4] = {pack16x2<kBf16>(sf[2 * kk][0], sf[2 * kk][1]),
-                             pack16x2<kBf16>(sf[2 * kk][2], sf[2 * kk][3]),
-                             pack16x2<kBf16>(sf[2 * kk + 1][0], sf[2 * kk + 1][1]),
-                             pack16x2<kBf16>(sf[2 * kk + 1][2], sf[2 * kk + 1][3])};
+  for (int kk = 0; kk < kNK; ++kk) {
+    const uint32_t a[4] = {pack16x2<kBf16>(sf[2 * kk][0], sf[2 * kk][1]),
+                           pack16x2<kBf16>(sf[2 * kk][2], sf[2 * kk][3]),
+                           pack16x2<kBf16>(sf[2 * kk + 1][0], sf[2 * kk + 1][1]),
+                           pack16x2<kBf16>(sf[2 * kk + 1][2], sf[2 * kk + 1][3])};
 #pragma unroll
-      for (int dt = 0; dt < kD / 8; dt += 2) {
-        uint32_t bv[4];
-        ldsm_x4_trans(v_base + 2 * ((kk * 16 + (mi & 1) * 8 + ri) * kRow + (dt + (mi >> 1)) * 8), bv);
-        mma16816<kBf16>(of[dt], a, bv[0], bv[1]);
-        mma16816<kBf16>(of[dt + 1], a, bv[2], bv[3]);
-      }
+    for (int dt = 0; dt < kD / 8; dt += 2) {
+      uint32_t bv[4];
+      ldsm_x4_trans(v_base + 2 * ((kk * 16 + (mi & 1) * 8 + ri) * kRow + (dt + (mi >> 1)) * 8), bv);
+      mma16816<kBf16>(of[dt], a, bv[0], bv[1]);
+      mma16816<kBf16>(of[dt + 1], a, bv[2], bv[3]);
     }
-    const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f, inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
+  }
+  const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f, inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
 #pragma unroll
-    for (int n = 0; n < kD / 8; ++n) {
-      const int col = 8 * n + 2 * t4;
-      if (g < Sq) *reinterpret_cast<uint32_t*>(ob + g * kD + col) = pack16x2<kBf16>(of[n][0] * inv0, of[n][1] * inv0);
-      if (g + 8 < Sq)
-        *reinterpret_cast<uint32_t*>(ob + (g + 8) * kD + col) = pack16x2<kBf16>(of[n][2] * inv1, of[n][3] * inv1);
-    }
+  for (int n = 0; n < kD / 8; ++n) {
+    const int col = 8 * n + 2 * t4;
+    if (g < Sq) *reinterpret_cast<uint32_t*>(ob + g * kD + col) = pack16x2<kBf16>(of[n][0] * inv0, of[n][1] * inv0);
+    if (g + 8 < Sq)
+      *reinterpret_cast<uint32_t*>(ob + (g + 8) * kD + col) = pack16x2<kBf16>(of[n][2] * inv1, of[n][3] * inv1);
   }
 }
 
