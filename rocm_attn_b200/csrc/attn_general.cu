@@ -63,19 +63,27 @@ int current_sm_count() {
 }
 
 // Raises the dynamic shared-memory limit of one kernel to `smem` bytes on the
-// current device, once per device; one static instance per kernel.
+// current device, once per device, and with `max_carveout` asks for the
+// largest shared-memory share of the SM (so shared memory does not cap the
+// CTAs per SM below what the registers allow); one static instance per
+// kernel.
 struct SmemOptIn {
   std::atomic<bool> done[kMaxDevices] = {};
   std::mutex mu;
   template <typename Kernel>
-  bool ensure(Kernel kern, int smem) {
-    if (smem <= 48 * 1024) return true;
+  bool ensure(Kernel kern, int smem, bool max_carveout = false) {
+    if (smem <= 48 * 1024 && !max_carveout) return true;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return false;
     if (done[dev].load(std::memory_order_acquire)) return true;
     std::lock_guard<std::mutex> g(mu);
     if (!done[dev].load(std::memory_order_relaxed)) {
-      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return false;
+      if (smem > 48 * 1024 &&
+          cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+        return false;
+      if (max_carveout && cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                               static_cast<int>(cudaSharedmemCarveoutMaxShared)) != cudaSuccess)
+        return false;
       done[dev].store(true, std::memory_order_release);
     }
     return true;
@@ -429,6 +437,16 @@ int launch_small_keys(const void* q, const void* k, const void* v, void* out, in
 // ---------------------------------------------------------------------------
 constexpr int kMmaWarps = 4;
 
+// CTAs per SM the short tensor-core kernel is compiled for.  The kernel is
+// bound by HBM latency, so more slices in flight per SM help: six CTAs (an
+// 80-register cap) where that compiles without spills (D = 64 with up to 16
+// keys, D <= 32 with up to 32; measured 5-7 % faster on the largest UnifoLM
+// 16-row shapes), otherwise no bound.
+template <int kD, int kNK>
+constexpr int small_mma_min_blocks() {
+  return ((kD == 64 && kNK == 1) || (kD <= 32 && kNK <= 2)) ? 6 : 1;
+}
+
 // 16-byte global -> shared copy that does not block the thread; with
 // valid = false nothing is read and the 16 bytes are zero-filled.
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
@@ -611,7 +629,7 @@ __device__ __forceinline__ uint16_t* small_mma_staging(unsigned char* smem, int 
 }
 
 template <bool kBf16, int kD, int kNK>
-__global__ void __launch_bounds__(kMmaWarps * 32) attn_small_mma_kernel(const uint16_t* __restrict__ q,
+__global__ void __launch_bounds__(kMmaWarps * 32, small_mma_min_blocks<kD, kNK>()) attn_small_mma_kernel(const uint16_t* __restrict__ q,
                                                                         const uint16_t* __restrict__ k,
                                                                         const uint16_t* __restrict__ v,
                                                                         uint16_t* __restrict__ o, bool causal,
@@ -647,7 +665,7 @@ struct SmallGroupArgs {
 };
 
 template <bool kBf16, int kD, int kNK>
-__global__ void __launch_bounds__(kMmaWarps * 32) attn_small_mma_group_kernel(const __grid_constant__ SmallGroupArgs a) {
+__global__ void __launch_bounds__(kMmaWarps * 32, small_mma_min_blocks<kD, kNK>()) attn_small_mma_group_kernel(const __grid_constant__ SmallGroupArgs a) {
   extern __shared__ __align__(16) unsigned char mma_smem[];
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
   uint16_t* sQ = small_mma_staging<kD, kNK>(mma_smem, warp);
@@ -675,7 +693,7 @@ int launch_small_mma_typed(const void* q, const void* k, const void* v, void* ou
   auto kern = attn_small_mma_kernel<kBf16, kD, kNK>;
   static SmemOptIn opt_in;
   const int sms = current_sm_count();
-  if (sms == 0 || !opt_in.ensure(kern, smem)) return -1;
+  if (sms == 0 || !opt_in.ensure(kern, smem, true)) return -1;
   const long long need = (static_cast<long long>(BH) + kMmaWarps - 1) / kMmaWarps;
   const unsigned grid = static_cast<unsigned>(need < 32LL * sms ? need : 32LL * sms);
   kern<<<grid, kMmaWarps * 32, smem, stream>>>(static_cast<const uint16_t*>(q), static_cast<const uint16_t*>(k),
@@ -690,7 +708,7 @@ int launch_small_mma_group_typed(const SmallGroupArgs& a, cudaStream_t stream) {
   auto kern = attn_small_mma_group_kernel<kBf16, kD, kNK>;
   static SmemOptIn opt_in;
   const int sms = current_sm_count();
-  if (sms == 0 || !opt_in.ensure(kern, smem)) return -1;
+  if (sms == 0 || !opt_in.ensure(kern, smem, true)) return -1;
   const long long need = (a.p[a.n - 1].slice_end + kMmaWarps - 1) / kMmaWarps;
   const unsigned grid = static_cast<unsigned>(need < 32LL * sms ? need : 32LL * sms);
   kern<<<grid, kMmaWarps * 32, smem, stream>>>(a);
