@@ -58,7 +58,7 @@ static int sm_count() {
 }
 
 // D=64 problems for 64-key blocks: with few blocks per unit the fixed cost of
-// a CTA (set-up, first block, epilogue) dominates, and three 64-key CTAs per
+// a CTA (set-up, first block, epilogue) dominates, and four 64-key CTAs per
 // SM hide more of it than two 128-key ones, provided the grid fills the SMs
 // more than twice over; with many blocks per unit, or a small grid, the
 // 128-key CTAs are faster.
@@ -160,7 +160,7 @@ static int prepare(const void* q, const void* k, const void* v, void* out, int B
   } else {
     c->route = Route::kTensorCore;
     // D=128: two-tile CTAs.  D=64: one-tile CTAs with 128-key blocks (two
-    // per SM), or with 64-key blocks (three per SM) for short key ranges.
+    // per SM), or with 64-key blocks (four per SM) for short key ranges.
     c->key = TcKey{dtype == ATTN_BF16, D, causal,
                    (D == 64 && d64_short_keys(BH * ((Sq + 127) / 128), Skv, causal)) ? 64 : 128};
   }
