@@ -13,7 +13,7 @@
 //
 // CTA work unit.  D=128: 256 query rows of one (batch, head) as two 128-row
 // Q tiles, one CTA per SM.  D=64: one 128-row tile, two CTAs per SM with
-// 128-key blocks, four with 64-key blocks (short key ranges).
+// 128-key blocks, four with 64-key blocks (grids of two or more CTAs per SM).
 // Warp roles (320 threads with two tiles, 192 with one):
 //   warps 0-3  softmax of Q tile 0 (thread <-> TMEM lane <-> query row)
 //   warps 4-7  softmax of Q tile 1 (two-tile CTAs)
