@@ -57,12 +57,13 @@ def test_cross_attention(attn, shape, dtype, causal):
     run_case(attn, shape, DT[dtype], causal)
 
 
-# D=64 problems the dispatcher sends to 64-key blocks (three CTAs per SM):
-# at least two CTAs per SM and short key ranges (<= 384 keys, <= 1024 causal),
-# with tails that are not multiples of 64 or 128.
+# D=64 problems the dispatcher sends to 64-key blocks (four CTAs per SM): grids
+# of at least two CTAs per SM, short and long key ranges, with tails that are
+# not multiples of 64 or 128.
 SHORT_KEYS = [Shape(16, 20, 160, 93, 64), Shape(8, 16, 384, 384, 64), Shape(8, 16, 512, 512, 64),
               Shape(8, 40, 200, 300, 64), Shape(16, 5, 2560, 351, 64),
-              Shape(64, 8, 128, 1, 64), Shape(16, 20, 300, 100, 64)]  # one key; more queries than keys
+              Shape(64, 8, 128, 1, 64), Shape(16, 20, 300, 100, 64),  # one key; more queries than keys
+              Shape(2, 16, 2048, 2048, 64), Shape(1, 40, 1000, 3000, 64)]  # long key ranges
 
 
 @pytest.mark.parametrize("dtype", ["fp16", "bf16"])
