@@ -145,10 +145,14 @@ static int prepare(const void* q, const void* k, const void* v, void* out, int B
     // Short sequences (a few dozen rows per head): one warp per (batch,
     // head) slice instead of a mostly empty 128- or 256-row tcgen05 unit.
     c->route = Route::kSmall;
-  } else if (mid_kernel_takes(Sq, Skv, D, dt)) {
+  } else if (mid_kernel_takes(Sq, Skv, D, dt) &&
+             !(D == 64 && Skv > 64 && d64_use_64_key_blocks(BH * ((Sq + 127) / 128)))) {
     // D = 16 / 32 at any length, and D = 64 with at most 64 queries and 256
     // keys: 64-row warp-level tensor-core tiles instead of 128-row tcgen05
-    // tiles.
+    // tiles.  At D = 64 only where the tcgen05 kernel would not run four
+    // 64-key CTAs per SM or the keys fit one 64-key chunk: with more keys on
+    // such grids the tcgen05 kernel measured 15-28 % faster (e.g. 64x16x48x256,
+    // 32x16x56x200), with 64 keys or fewer 15-25 % slower.
     c->route = Route::kMid;
   } else if (dtype == ATTN_F32 || (D != 64 && D != 128) || !aligned(out, 16)) {
     // The tensor-core kernel takes fp16/bf16 with D in {64, 128} and
