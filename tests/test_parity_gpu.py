@@ -63,7 +63,8 @@ def test_cross_attention(attn, shape, dtype, causal):
 SHORT_KEYS = [Shape(16, 20, 160, 93, 64), Shape(8, 16, 384, 384, 64), Shape(8, 16, 512, 512, 64),
               Shape(8, 40, 200, 300, 64), Shape(16, 5, 2560, 351, 64),
               Shape(64, 8, 128, 1, 64), Shape(16, 20, 300, 100, 64),  # one key; more queries than keys
-              Shape(2, 16, 2048, 2048, 64), Shape(1, 40, 1000, 3000, 64)]  # long key ranges
+              Shape(2, 16, 2048, 2048, 64), Shape(1, 40, 1000, 3000, 64),  # long key ranges
+              Shape(64, 16, 48, 256, 64), Shape(32, 16, 56, 200, 64)]  # short queries, more than 64 keys
 
 
 @pytest.mark.parametrize("dtype", ["fp16", "bf16"])
